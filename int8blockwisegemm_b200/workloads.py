@@ -1,0 +1,131 @@
+"""Seeded synthetic inputs for the benchmark configurations.
+
+The reference publishes no dataset; every configuration is synthetic.  All
+tensors are drawn from one CPU ``torch.Generator`` in a fixed order so the
+GPU path, the expert-parallel path and the CPU oracle see bit-identical
+inputs.  Shapes and distributions follow the reference benchmark's problem
+definition (bench_int8_hybrid_moe.py:74-95,199-253) with the scale
+distributions of the benchmark configurations:
+
+  hidden       ~ N(0, 1)                       [T, K]  (bf16, fp16 for "large")
+  router       logits ~ N(0, 1) [T, E] (+ per-expert bias), top-k ids,
+               weights = softmax over the selected (unbiased) logits
+  w13 / w2     int8 uniform in [-127, 127]     [E, 2N, K] / [E, K, N]
+  Q scales     int32 uniform in [1, 16]        [E, Nout/64, Kb]
+  F scales     fp32 lognormal(-6, 0.5)         [E, Nout/64, ceil(Kb/sg)]
+
+This module imports only torch so it can be loaded on its own.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass(frozen=True)
+class MoEConfig:
+    name: str
+    T: int            # tokens
+    K: int            # hidden
+    N: int            # intermediate (w13 output is 2N)
+    E: int            # experts
+    topk: int
+    dtype: str = "bf16"
+    sg: int = 256     # super-group size (K-blocks per F)
+    q_max: int = 16
+    quant_block: int = 128
+    router: str = "uniform"   # uniform | bias | zipf
+    seed: int = 0
+    f_mu: float = -6.0        # log-mean of the weight F scales
+    extra: dict = field(default_factory=dict, compare=False)
+
+    @property
+    def R(self) -> int:
+        return self.T * self.topk
+
+    def gemm_ops(self) -> int:
+        """Algorithmic int8 ops of both GEMMs (2*R*Nout*K each)."""
+        return 2 * self.R * (2 * self.N) * self.K + 2 * self.R * self.K * self.N
+
+
+CONFIGS = {
+    # tiny CPU-runnable reference case.
+    "tiny": MoEConfig("tiny", T=64, K=256, N=128, E=8, topk=2, sg=2),
+    # default Qwen3-MoE-like benchmark shape (the headline).
+    "default": MoEConfig("default", T=8192, K=2048, N=512, E=256, topk=8),
+    # decode regime.
+    "decode": MoEConfig("decode", T=128, K=2048, N=512, E=256, topk=8),
+    # large experts, fp16 activations, mildly biased router.
+    "large": MoEConfig("large", T=16384, K=4096, N=1536, E=128, topk=8, dtype="fp16",
+                       router="bias"),
+    # skewed routing (hottest expert ~10x mean load).
+    "skewed": MoEConfig("skewed", T=32768, K=2048, N=512, E=256, topk=8, router="zipf"),
+    # Small edge cases used by the parity tests.
+    "ragged": MoEConfig("ragged", T=48, K=160, N=96, E=6, topk=2, sg=2, seed=3,
+                        extra={"dead_experts": (3,)}),
+    # fp16 with smaller weight F scales so the SiLU product stays finite.
+    "tm128": MoEConfig("tm128", T=160, K=256, N=128, E=4, topk=2, dtype="fp16", sg=1, seed=5,
+                       f_mu=-9.0),
+    "mid": MoEConfig("mid", T=512, K=512, N=256, E=16, topk=4, seed=7),
+}
+
+TORCH_DTYPE = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
+
+
+def _zipf_bias(gen: torch.Generator, T: int, E: int, topk: int, target: float = 10.0):
+    """Per-expert bias alpha*log(p_pi(e)) with p_r ~ r^-1.1, alpha bisected so
+    that max expert load / mean load ~= target on the seeded sample."""
+    perm = torch.randperm(E, generator=gen)
+    ranks = torch.arange(1, E + 1, dtype=torch.float64)
+    logp = (-1.1 * torch.log(ranks))
+    logp = logp - torch.logsumexp(logp, 0)
+    base = logp[perm].float()
+    probe = torch.randn(min(T, 8192), E, generator=gen)
+    lo, hi = 0.0, 8.0
+    for _ in range(40):
+        a = 0.5 * (lo + hi)
+        ids = torch.topk(probe + a * base, topk, dim=-1).indices
+        load = torch.bincount(ids.reshape(-1), minlength=E).float()
+        ratio = (load.max() / load.mean()).item()
+        if ratio < target:
+            lo = a
+        else:
+            hi = a
+    return 0.5 * (lo + hi) * base
+
+
+def make_inputs(cfg: MoEConfig, seed: int | None = None) -> dict:
+    """Generate every input tensor of one forward on the CPU."""
+    g = torch.Generator().manual_seed(cfg.seed if seed is None else seed)
+    T, K, N, E, k = cfg.T, cfg.K, cfg.N, cfg.E, cfg.topk
+    dt = TORCH_DTYPE[cfg.dtype]
+    hidden = torch.randn(T, K, generator=g).to(dt)
+    logits = torch.randn(T, E, generator=g)
+    if cfg.router == "bias":
+        bias = torch.randn(E, generator=g) * 0.5
+    elif cfg.router == "zipf":
+        bias = _zipf_bias(g, T, E, k)
+    else:
+        bias = torch.zeros(E)
+    biased = logits + bias
+    for e in cfg.extra.get("dead_experts", ()):
+        biased[:, e] = -1e30
+    top = torch.topk(biased, k, dim=-1)
+    topk_ids = top.indices.to(torch.int32)
+    sel = torch.gather(logits, 1, top.indices)
+    topk_weights = torch.softmax(sel, dim=-1).float()
+    kb1 = math.ceil(K / cfg.quant_block)
+    kb2 = math.ceil(N / cfg.quant_block)
+    w13 = torch.randint(-127, 128, (E, 2 * N, K), generator=g, dtype=torch.int8)
+    w2 = torch.randint(-127, 128, (E, K, N), generator=g, dtype=torch.int8)
+    q13 = torch.randint(1, 17, (E, math.ceil(2 * N / 64), kb1), generator=g, dtype=torch.int32)
+    f13 = torch.empty(E, math.ceil(2 * N / 64), math.ceil(kb1 / cfg.sg)).log_normal_(
+        cfg.f_mu, 0.5, generator=g)
+    q2 = torch.randint(1, 17, (E, math.ceil(K / 64), kb2), generator=g, dtype=torch.int32)
+    f2 = torch.empty(E, math.ceil(K / 64), math.ceil(kb2 / cfg.sg)).log_normal_(
+        cfg.f_mu, 0.5, generator=g)
+    return dict(hidden=hidden, topk_ids=topk_ids, topk_weights=topk_weights, w13=w13, w2=w2,
+                w13_q=q13, w13_f=f13, w2_q=q2, w2_f=f2)
