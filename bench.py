@@ -1,0 +1,424 @@
+#!/usr/bin/env python3
+"""Benchmark of the INT8 hybrid MoE forward on B200 (BASELINE metric:
+"MoE fwd ms & INT8 TOPS (M=8192,K=2048,N=512,E=256,top8)").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config default|decode|large|skewed|...] [--no-cpu-baseline]
+
+One step = one forward pass (routing -> permute+quant -> w13 GEMM ->
+SiLU*up+requant -> w2 GEMM -> weighted unpermute) over one batch of the
+configuration's tokens.  ``value`` is whole-job INT8 TOPS (GEMM ops of all
+ranks / max-over-ranks device time); ``ms_per_step`` is the forward latency.
+Inputs are synthetic (seeded, BASELINE distributions) and resident in HBM;
+the whole forward is replayed from a CUDA graph.  ``e2e`` times the public
+entry point (cutlass_runner._run_cutlass_int8_hybrid_grouped_moe) called
+eagerly with the per-step inputs copied from pinned host memory and the
+output copied back inside the timed region.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own batch of
+the configuration (data-parallel replicas, weak scaling); the timed region is
+bracketed by barriers and the reported time is the max over ranks.
+
+``--impl reference`` times the CPU restatement of the reference path
+(oracle/ref_cpu.py, numpy on the host cores) on a bounded token sample of the
+same workload, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "MoE fwd INT8 TOPS (M=8192,K=2048,N=512,E=256,top8)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="default")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="run N eager forwards only (for ncu launch lists); no JSON")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def load_workloads():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_bench_workloads",
+                                                  ROOT / "int8blockwisegemm_b200" / "workloads.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["_bench_workloads"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+            except Exception:
+                pass
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        load = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU arm (oracle port on the host cores)
+# ---------------------------------------------------------------------------
+
+def cpu_forward_sample(cfg, inp, n_tokens: int):
+    from oracle import ref_cpu as ref
+    npi = {k: (v.float().numpy() if v.is_floating_point() else v.numpy()) for k, v in inp.items()}
+    T = min(n_tokens, cfg.T)
+    t0 = time.perf_counter()
+    ref.moe_forward(npi["hidden"][:T], npi["w13"], npi["w2"], npi["topk_ids"][:T],
+                    npi["topk_weights"][:T], npi["w13_q"], npi["w13_f"], npi["w2_q"], npi["w2_f"],
+                    dtype=cfg.dtype, global_num_experts=cfg.E, super_group_size=cfg.sg,
+                    q_max=cfg.q_max)
+    dt = time.perf_counter() - t0
+    ops = T * cfg.topk * (2 * 2 * cfg.N * cfg.K + 2 * cfg.K * cfg.N)
+    return ops, dt, T
+
+
+def run_reference(args, world, rank):
+    wl = load_workloads()
+    cfg = wl.CONFIGS[args.config]
+    if rank != 0:
+        return
+    inp = wl.make_inputs(cfg)
+    sample = int(os.environ.get("I8MOE_CPU_SAMPLE_TOKENS", "1024"))
+    for _ in range(args.warmup):
+        cpu_forward_sample(cfg, inp, sample)
+    tot_ops, tot_t = 0, 0.0
+    for _ in range(args.steps):
+        ops, dt, T = cpu_forward_sample(cfg, inp, sample)
+        tot_ops += ops
+        tot_t += dt
+    tops = tot_ops / tot_t / 1e12
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * tot_t / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: T={cfg.T},K={cfg.K},N={cfg.N},E={cfg.E},"
+                               f"top{cfg.topk},{cfg.dtype}", "sample_tokens": T},
+        "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": cores, "kind": "port",
+                         "sample": f"first {T} of {cfg.T} tokens of the {cfg.name} workload, "
+                                   f"numpy oracle (oracle/ref_cpu.py), BLAS threads = {cores}"},
+        "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def make_problem(cfg, inp, dev):
+    import int8blockwisegemm_b200 as pkg
+    r = pkg.cutlass_runner
+    r._USE_FUSED_PERMUTE_QUANT_W1 = True   # BASELINE: fused permute+quant on
+    r._USE_FUSED_SILU_QUANT_W2 = True      # BASELINE: fused SiLU+quant on
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16}[cfg.dtype]
+    T, k = inp["topk_ids"].shape
+    R = T * k
+    K, N = cfg.K, cfg.N
+    st = dict(
+        hidden=inp["hidden"].to(dev), topk_ids=inp["topk_ids"].to(dev),
+        topk_weights=inp["topk_weights"].to(dev),
+        w1=inp["w13"].to(dev), w2=inp["w2"].to(dev), w1_qscale=inp["w13_q"].to(dev),
+        w1_fscale=inp["w13_f"].to(dev), w2_qscale=inp["w2_q"].to(dev),
+        w2_fscale=inp["w2_f"].to(dev),
+        workspace13=torch.empty(R, max(2 * N, K), dtype=dt, device=dev),
+        workspace2=torch.empty(R, max(N, K), dtype=dt, device=dev),
+        output=torch.empty(T, K, dtype=dt, device=dev))
+
+    def fwd(**over):
+        a = dict(st)
+        a.update(over)
+        r._run_cutlass_int8_hybrid_grouped_moe(
+            output=a["output"], hidden_states=a["hidden"], w1=a["w1"], w2=a["w2"],
+            topk_ids=a["topk_ids"], topk_weights=a["topk_weights"],
+            activation=pkg.activation.MoEActivation.SILU, global_num_experts=cfg.E,
+            expert_map=None, w1_qscale=a["w1_qscale"], w1_fscale=a["w1_fscale"],
+            w2_qscale=a["w2_qscale"], w2_fscale=a["w2_fscale"], workspace13=a["workspace13"],
+            workspace2=a["workspace2"], quant_block_size=cfg.quant_block,
+            super_group_size=cfg.sg, q_max=cfg.q_max, _trace=a.get("_trace"))
+
+    return pkg, st, fwd
+
+
+def time_w13_gemm(pkg, cfg, st, tr, iters=20):
+    """Average device time of the w13 grouped GEMM launch (dominant kernel),
+    CUDA events on the launching stream."""
+    tm = tr["tile_m"]
+    fn = (pkg.ops.cutlass_int8_blockwise_hybrid_grouped if tm == 128
+          else pkg.ops.cutlass_int8_blockwise_hybrid_grouped_small)
+    args = (tr["a1q"], tr["a1_Q"], tr["a1_F"], st["w1"], st["w1_qscale"], st["w1_fscale"],
+            tr["expert_offsets"], tr["problem_sizes1"], st["workspace13"][: tr["a1q"].shape[0] *
+            2 * cfg.N].view(-1, 2 * cfg.N), cfg.quant_block, cfg.sg, tr["a1_so"])
+    for _ in range(3):
+        fn(*args)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(iters):
+        fn(*args)
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e-3
+
+
+def run_ours(args, world, rank, local):
+    wl = load_workloads()
+    cfg = wl.CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    inp = wl.make_inputs(cfg, seed=cfg.seed + rank)
+    pkg, st, fwd = make_problem(cfg, inp, dev)
+    T, k = inp["topk_ids"].shape
+    R = T * k
+    ops_per_step = 2 * R * (2 * cfg.N) * cfg.K + 2 * R * cfg.K * cfg.N
+
+    if args.profile_steps:
+        for _ in range(args.profile_steps):
+            fwd()
+        torch.cuda.synchronize()
+        return
+
+    # ---- device-timed forward (CUDA graph replay) ----
+    for _ in range(max(1, args.warmup)):
+        fwd()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fwd()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+        barrier(world)
+    dt = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    clocks = clk.summary()
+    ms = dt / args.steps * 1e3
+    tops = world * ops_per_step * args.steps / dt / 1e12
+
+    # ---- end-to-end through the public API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        h_hidden = inp["hidden"].pin_memory()
+        h_ids = inp["topk_ids"].pin_memory()
+        h_w = inp["topk_weights"].pin_memory()
+        h_out = torch.empty_like(st["output"], device="cpu").pin_memory()
+        d_hidden = torch.empty_like(st["hidden"])
+        d_ids = torch.empty_like(st["topk_ids"])
+        d_w = torch.empty_like(st["topk_weights"])
+
+        def e2e_step():
+            d_hidden.copy_(h_hidden, non_blocking=True)
+            d_ids.copy_(h_ids, non_blocking=True)
+            d_w.copy_(h_w, non_blocking=True)
+            fwd(hidden=d_hidden, topk_ids=d_ids, topk_weights=d_w)
+            h_out.copy_(st["output"], non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        barrier(world)
+        dte = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+        bi = h_hidden.numel() * h_hidden.element_size() + h_ids.numel() * 4 + h_w.numel() * 4
+        bo = h_out.numel() * h_out.element_size()
+        e2e = {"value": world * ops_per_step * args.steps / dte / 1e12, "unit": "TOPS",
+               "ms_per_step": dte / args.steps * 1e3, "h2d_bytes_per_step": bi,
+               "d2h_bytes_per_step": bo}
+
+    # ---- roofline of the dominant kernel (w13 grouped GEMM) ----
+    tr = {}
+    fwd(_trace=tr)
+    torch.cuda.synchronize()
+    t_gemm = time_w13_gemm(pkg, cfg, st, tr)
+    eft = tr["eft"].cpu()
+    e_hit = int(((eft[1:] - eft[:-1]) > 0).sum())
+    n_sb = -(-2 * cfg.N // 64)
+    kb = -(-cfg.K // 128)
+    rows_s = tr["a1_Q"].shape[0]
+    gemm_bytes = (R * cfg.K + e_hit * 2 * cfg.N * cfg.K + R * 2 * cfg.N * 2
+                  + e_hit * n_sb * kb * 4 * 2 + rows_s * kb * 4)
+    gemm_ops = 2 * R * 2 * cfg.N * cfg.K
+    hbm, bf16, src = measured_peaks()
+    achieved = gemm_bytes / t_gemm / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(f"{cfg.name}/w13_gemm")
+
+    gpu_launches = 8 * args.steps
+    line = {
+        "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: T={cfg.T},K={cfg.K},N={cfg.N},E={cfg.E},"
+                               f"top{cfg.topk},{cfg.dtype} activations, fused permute+quant "
+                               f"and SiLU+quant",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "global_batch_tokens": world * cfg.T,
+                   "l2": "no flush: weights+activations (~1.2 GB/step) exceed the 126 MB L2",
+                   "timing": "CUDA-graph replay of the whole forward, CUDA events, max over ranks"},
+        "clocks": clocks,
+        "gpu_launches": gpu_launches,
+        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel (w13)",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": src, "traffic": traffic,
+                     "algorithmic_bytes": gemm_bytes, "launch_ms": t_gemm * 1e3,
+                     "int8_tops": gemm_ops / t_gemm / 1e12},
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = int(os.environ.get("I8MOE_CPU_SAMPLE_TOKENS", "2048"))
+        ops_c, dt_c, T_c = cpu_forward_sample(cfg, inp, sample)
+        line["cpu_baseline"] = {
+            "value": ops_c / dt_c / 1e12, "unit": "TOPS", "cores": os.cpu_count(),
+            "kind": "port", "seconds": dt_c,
+            "sample": f"first {T_c} of {cfg.T} tokens of the {cfg.name} workload through the "
+                      f"numpy oracle (oracle/ref_cpu.py)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,217 @@
+/*
+ * i8moe.h -- C ABI of libi8moe.so, the sm_100a (B200) implementation of the
+ * INT8 hybrid MoE forward path of PatchouliTIS/INT8BlockwiseGEMM.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer unless stated otherwise; every tensor
+ *    is dense and row-major.  The caller allocates every output (the
+ *    reference ops are all out-parameter style).
+ *  - Every entry point launches asynchronously on `stream` (a cudaStream_t)
+ *    on the current device and never synchronises.
+ *  - Return value: I8MOE_OK (0) or a negative I8MOE_ERR_* code;
+ *    i8moe_last_error() then returns a message (per calling thread).
+ *  - Kernels never trap.  A device-side wait that times out or an index that
+ *    fails a bounds check sets a bit in a per-device error word that
+ *    i8moe_device_error() reads.
+ *  - Reference locations are given as path:line inside the reference
+ *    project.
+ */
+#ifndef I8MOE_H_
+#define I8MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* i8moe_stream_t; /* cudaStream_t */
+
+enum {
+  I8MOE_OK = 0,
+  I8MOE_ERR_INVALID = -1,     /* bad argument (the reference's TORCH_CHECK cases) */
+  I8MOE_ERR_CUDA = -2,        /* a CUDA runtime / driver call failed */
+  I8MOE_ERR_UNSUPPORTED = -3, /* device is not sm_100 or shape outside supported range */
+};
+
+/* Element types of activations / outputs.  I8MOE_S32 is accepted only as a
+ * GEMM output: it stores the raw int32 accumulator W (before the float
+ * epilogue) for bit-exact verification. */
+enum { I8MOE_BF16 = 0, I8MOE_FP16 = 1, I8MOE_FP32 = 2, I8MOE_S32 = 3 };
+
+/* ---------------------------------------------------------------- misc */
+
+int i8moe_abi_version(void);
+const char* i8moe_last_error(void);
+/* Reads (and with clear != 0 resets) the device error word of `device`. */
+int i8moe_device_error(int device, uint32_t* word, int clear);
+/* Replaces moe_permute_unpermute_supported
+ * (csrc/moe_permute_unpermute_op.cu:258-264, schema csrc/torch_bindings.cpp:127):
+ * 1, because the library is built with CUDA >= 12 (no device needed). */
+int i8moe_moe_permute_unpermute_supported(void);
+
+/* ------------------------------------------------------------- routing */
+
+/* Bytes of scratch the routing entry points need for n_rows = n_token*topk
+ * keys of n_expert experts. */
+size_t i8moe_route_workspace_size(int64_t n_rows, int64_t n_expert);
+
+/* Replaces moe_permute_metadata (csrc/moe_permute_unpermute_op.cu:81-132,
+ * schema csrc/torch_bindings.cpp:116-120).  Stable sort of the expanded rows
+ * by expert id:
+ *   expert_first_token_offset[n_local_expert+1] (int64),
+ *   inv_permuted_idx[n_token*topk]  (source expanded row -> destination),
+ *   permuted_idx[n_token*topk]      (destination -> source; only rows below
+ *       expert_first_token_offset[n_local_expert] are written when
+ *       expert_map != NULL, every row otherwise).
+ * token_expert_indices supplies the value sorted with each key (the
+ * reference passes arange).  expert_map (nullable, [n_expert]) remaps
+ * global ids for expert parallelism as the reference does.  `workspace` must
+ * hold i8moe_route_workspace_size() bytes. */
+int i8moe_moe_permute_metadata(const int32_t* topk_ids, const int32_t* token_expert_indices,
+                               const int32_t* expert_map, int64_t n_token, int64_t topk,
+                               int64_t n_expert, int64_t n_local_expert,
+                               int64_t* expert_first_token_offset, int32_t* inv_permuted_idx,
+                               int32_t* permuted_idx, void* workspace, size_t workspace_bytes,
+                               i8moe_stream_t stream);
+
+/* Fused-forward variant of i8moe_moe_permute_metadata (no reference
+ * counterpart; it replaces the host-side torch glue of the reference runner,
+ * int8_hybrid_moe/cutlass_runner.py:136-143 and the scale-offset cumsum of
+ * int8_hybrid_moe/quant.py:391-395).  Besides the routing maps it writes
+ *   expert_offsets [n_local+1] int32, problem_sizes13 / problem_sizes2
+ *   [n_local, 3] int32 = (M_e, n_out1, k1) / (M_e, n_out2, k2), and
+ *   scale_offsets [n_local+1] int32 = exclusive cumsum of ceil(M_e/tile_m),
+ * from the same kernels, so the forward needs no extra launches. */
+int i8moe_moe_route_for_gemm(const int32_t* topk_ids, const int32_t* token_expert_indices,
+                             const int32_t* expert_map, int64_t n_token, int64_t topk,
+                             int64_t n_expert, int64_t n_local_expert,
+                             int64_t* expert_first_token_offset, int32_t* inv_permuted_idx,
+                             int32_t* permuted_idx, int32_t* expert_offsets,
+                             int32_t* problem_sizes13, int32_t* problem_sizes2,
+                             int32_t* scale_offsets, int64_t n_out1, int64_t k1, int64_t n_out2,
+                             int64_t k2, int64_t tile_m, void* workspace,
+                             size_t workspace_bytes, i8moe_stream_t stream);
+
+/* Replaces moe_permute (csrc/moe_permute_unpermute_op.cu:10-79, schema
+ * csrc/torch_bindings.cpp:109-114): the metadata above plus the row gather
+ * permuted_input[d] = input[permuted_idx[d] / topk] (expandInputRowsKernel,
+ * permute_unpermute_kernels/moe_permute_unpermute_kernel.inl:3-78). */
+int i8moe_moe_permute(const void* input, int dtype, int64_t n_hidden, const int32_t* topk_ids,
+                      const int32_t* token_expert_indices, const int32_t* expert_map,
+                      int64_t n_token, int64_t topk, int64_t n_expert, int64_t n_local_expert,
+                      void* permuted_input, int64_t* expert_first_token_offset,
+                      int32_t* inv_permuted_idx, int32_t* permuted_idx, void* workspace,
+                      size_t workspace_bytes, i8moe_stream_t stream);
+
+/* Replaces moe_unpermute (csrc/moe_permute_unpermute_op.cu:134-169,
+ * finalizeMoeRoutingKernel moe_permute_unpermute_kernel.inl:132-206):
+ *   out[t] = dtype( sum_j fma(topk_weights[t,j], permuted[inv[t,j]], acc) )
+ * skipping rows >= expert_first_token_offset[n_local_expert] when that
+ * pointer is non-NULL. */
+int i8moe_moe_unpermute(const void* permuted_hidden, int dtype, const float* topk_weights,
+                        const int32_t* inv_permuted_idx,
+                        const int64_t* expert_first_token_offset, int64_t n_local_expert,
+                        int64_t n_token, int64_t topk, int64_t n_hidden, void* out,
+                        i8moe_stream_t stream);
+
+/* ---------------------------------------------------------- activation */
+
+/* Replaces silu_and_mul (csrc/activation_kernels.cu:260-265):
+ * out[r, i] = dtype(silu(x[r, i])) * x[r, d + i], x is [n_rows, 2d]. */
+int i8moe_silu_and_mul(void* out, const void* input, int dtype, int64_t n_rows, int64_t d,
+                       i8moe_stream_t stream);
+
+/* ---------------------------------------------------------------- quant */
+
+/* Scale rows of one grouped quant: scale_offsets[E+1] = exclusive cumsum of
+ * ceil((expert_offsets[e+1]-expert_offsets[e]) / tile_m)
+ * (int8_hybrid_moe/quant.py:238-242). */
+int i8moe_scale_offsets(const int32_t* expert_offsets, int64_t n_expert, int64_t tile_m,
+                        int32_t* scale_offsets, i8moe_stream_t stream);
+
+/* Per-(expert M-tile x 128-K block) absmax INT8 quantisation with the
+ * two-level (Q int32, F fp32) scale factorisation folded in.
+ *
+ * Replaces, for the three activation sources:
+ *   i8moe_quant_grouped  -- moe_kernel_quantize_input_int8_hybrid_grouped
+ *                           (int8_hybrid_moe/quant.py:147-277), A is [M, K]
+ *   i8moe_quant_permute  -- fused_permute_quant_int8_hybrid_grouped
+ *                           (quant.py:284-433), rows hidden[permuted_idx/topk]
+ *   i8moe_quant_silu     -- fused_silu_quant_int8_hybrid_grouped
+ *                           (quant.py:440-579), x = silu(gate) * up of mm1
+ *                           [M, 2K]
+ * followed by quantize_scales_for_hybrid (quant.py:52-140).
+ * Outputs: qA [M, K] int8 (rows outside every expert untouched),
+ *          Q [rows_upper, Kb] int32, F [rows_upper, ceil(Kb/super_group)],
+ *          where only the first scale_offsets[E] rows are written;
+ *          scale_offsets [E+1] int32 (computed here when
+ *          `scale_offsets_ready` == 0, read as given otherwise).
+ * block_k must be 128; K % 8 == 0. */
+int i8moe_quant_grouped(const void* A, int dtype, int64_t M, int64_t K,
+                        const int32_t* expert_offsets, int64_t n_expert, int64_t tile_m,
+                        int64_t block_k, int64_t q_max, int64_t super_group_size, int8_t* qA,
+                        int32_t* Q, float* F, int32_t* scale_offsets, int scale_offsets_ready,
+                        i8moe_stream_t stream);
+int i8moe_quant_permute(const void* hidden, int dtype, int64_t n_token, int64_t K,
+                        const int32_t* permuted_idx, int64_t M, int64_t topk,
+                        const int32_t* expert_offsets, int64_t n_expert, int64_t tile_m,
+                        int64_t block_k, int64_t q_max, int64_t super_group_size, int8_t* qA,
+                        int32_t* Q, float* F, int32_t* scale_offsets, int scale_offsets_ready,
+                        i8moe_stream_t stream);
+int i8moe_quant_silu(const void* mm1, int dtype, int64_t M, int64_t N,
+                     const int32_t* expert_offsets, int64_t n_expert, int64_t tile_m,
+                     int64_t block_k, int64_t q_max, int64_t super_group_size, int8_t* qA,
+                     int32_t* Q, float* F, int32_t* scale_offsets, int scale_offsets_ready,
+                     i8moe_stream_t stream);
+
+/* Replaces quantize_scales_for_hybrid (int8_hybrid_moe/quant.py:52-140) on a
+ * standalone fp32 scale matrix [rows, kb]. */
+int i8moe_quantize_scales(const float* scale, int64_t rows, int64_t kb, int64_t q_max,
+                          int64_t super_group_size, int32_t* Q, float* F,
+                          i8moe_stream_t stream);
+
+/* ---------------------------------------------------------------- GEMMs */
+
+/* Replaces cutlass_int8_blockwise_hybrid_grouped{,_small}{,_bias}
+ * (csrc/int8_hybrid_grouped_gemm.cu:757-805, schemas
+ * csrc/torch_bindings.cpp:80-106).  tcgen05 kind::i8 persistent grouped GEMM:
+ *   W[r,n]   = sum_qb (a_qscale[s,qb] * b_qscale[e,n/64,qb]) *
+ *              sum_{k in qb} a_q[r,k] * b_q[e,n,k]        (int32, wrapping)
+ *   out[r,n] = out_dtype( float(W) * (a_fscale[s,0] * b_fscale[e,n/64,0]) [+ bias] )
+ * with s = scale_offsets[e] + (r - expert_offsets[e]) / tile_m
+ * (tile_m 128 = default variant, 64 = _small variant).  a_q [sum_m, k],
+ * b_q [n_expert, n, k], out [sum_m, n]; problem_sizes [n_expert, 3]
+ * (M_e, n, k).  scale_offsets may be NULL (then derived from
+ * problem_sizes); bias NULL or fp32 [n] (bias_stride 0) / [n_expert, n]
+ * (bias_stride n).  out_dtype I8MOE_BF16 (the reference's only output),
+ * I8MOE_FP16, or I8MOE_S32 (raw W, no bias).  Requires k % 32 == 0, n % 8 == 0,
+ * quant_block_size % 128 == 0. */
+int i8moe_hybrid_grouped_gemm(const int8_t* a_q, const int32_t* a_qscale, const float* a_fscale,
+                              int64_t a_scale_rows, const int8_t* b_q, const int32_t* b_qscale,
+                              const float* b_fscale, const int32_t* expert_offsets,
+                              const int32_t* problem_sizes, const int32_t* scale_offsets,
+                              const float* bias, int64_t bias_stride, void* out, int out_dtype,
+                              int64_t n_expert, int64_t sum_m, int64_t n, int64_t k,
+                              int64_t quant_block_size, int64_t super_group_size,
+                              int64_t tile_m, i8moe_stream_t stream);
+
+/* Replaces cutlass_int8_grouped_mm (csrc/int8_grouped_gemm.cu:106-220,
+ * schema csrc/torch_bindings.cpp:75-78):
+ *   out[r,n] = out_dtype(float(sum_k a[r,k]*b[e,n,k]) * alpha_r)
+ * alpha_r = alpha (per tensor; the reference's float(a_scale*b_scale)), or,
+ * when a_row_scale and b_expert_scale are both non-NULL,
+ * alpha_r = a_row_scale[r] * b_expert_scale[e] (per-token x per-expert
+ * extension).  No host synchronisation. */
+int i8moe_int8_grouped_mm(const int8_t* a, const int8_t* b, void* out, int out_dtype,
+                          float alpha, const float* a_row_scale, const float* b_expert_scale,
+                          const int32_t* expert_offsets, const int32_t* problem_sizes,
+                          int64_t n_expert, int64_t sum_m, int64_t n, int64_t k,
+                          i8moe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* I8MOE_H_ */

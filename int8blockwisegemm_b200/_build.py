@@ -1,0 +1,97 @@
+"""Build libi8moe.so in-tree with nvcc for sm_100a.
+
+    python -m int8blockwisegemm_b200._build [--force] [--verbose]
+
+Objects go to int8blockwisegemm_b200/_build/ (git-ignored); the shared
+library is written next to this file so it travels with the source tree.
+cudart is linked statically and the driver entry point needed for TMA
+descriptors is resolved at run time, so the library loads on machines
+without a GPU driver (calls then fail with I8MOE_ERR_CUDA).
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = PKG / "_build"
+LIB = PKG / "libi8moe.so"
+INCLUDE = ROOT / "include"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
+    "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}",
+]
+
+
+def nvcc() -> str:
+    cand = os.environ.get("NVCC") or shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    return cand
+
+
+def sources():
+    return sorted(CSRC.glob("*.cu"))
+
+
+def _headers_mtime() -> float:
+    hs = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
+    return max((h.stat().st_mtime for h in hs), default=0.0)
+
+
+def _compile(src: Path, force: bool, verbose: bool, extra: list[str]) -> Path:
+    obj = BUILD / (src.stem + ".o")
+    if (not force and obj.exists()
+            and obj.stat().st_mtime >= max(src.stat().st_mtime, _headers_mtime())):
+        return obj
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src.name}:\n{res.stdout}\n{res.stderr}")
+    if verbose and (res.stdout or res.stderr):
+        print(res.stdout + res.stderr, flush=True)
+    return obj
+
+
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    extra = list(extra or [])
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, force, verbose, extra), sources()))
+    newest = max(o.stat().st_mtime for o in objs)
+    if force or not LIB.exists() or LIB.stat().st_mtime < newest:
+        tmp = LIB.with_suffix(".so.tmp")
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+        os.replace(tmp, LIB)
+    return LIB
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--ptxas-info", action="store_true", help="print registers/spills per kernel")
+    args = ap.parse_args(argv)
+    extra = ["-Xptxas", "-v"] if args.ptxas_info else []
+    lib = build(force=args.force or args.ptxas_info, verbose=args.verbose or args.ptxas_info,
+                extra=extra)
+    print(lib)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,142 @@
+"""Activation quantisation entry points with the reference's signatures and
+return values (int8_hybrid_moe/quant.py:99-140, 212-277, 360-433, 514-579),
+computed by the sm_100a cluster kernels of libi8moe (csrc/quant.cu): the
+per-(expert M-tile x 128-K block) absmax INT8 quantisation and the two-level
+(Q int32, F fp32) scale factorisation run in one launch.
+
+Each function returns ``(qA, Q_A, F_A, scale_offsets_i32)`` with
+Q_A [cdiv(M, tile_m) + E, K_blocks] and F_A [same rows, num_super_groups];
+only the first scale_offsets[E] rows are written (the reference leaves the
+remaining rows of its ``torch.empty`` scale buffer unset as well).
+"""
+
+from __future__ import annotations
+
+from math import prod
+
+import torch
+
+from ._lib import BF16, FP16, FP32, call
+
+_DT = {torch.bfloat16: BF16, torch.float16: FP16, torch.float32: FP32}
+
+
+def cdiv(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
+def _resize_cache(x: torch.Tensor, v: tuple[int, ...]) -> torch.Tensor:
+    """Shrink a workspace and view it with shape ``v`` (quant.py:26-29)."""
+    assert prod(v) <= x.numel(), f"{v} ({prod(v)}) <= {x.shape} ({x.numel()})"
+    return x.flatten()[: prod(v)].view(*v)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _outputs(M: int, K: int, E: int, tile_m: int, block_k: int, super_group_size: int, device):
+    kb = cdiv(K, block_k)
+    rows = cdiv(M, tile_m) + E
+    qA = torch.empty((M, K), dtype=torch.int8, device=device)
+    Q = torch.empty((rows, kb), dtype=torch.int32, device=device)
+    F = torch.empty((rows, cdiv(kb, super_group_size)), dtype=torch.float32, device=device)
+    return qA, Q, F
+
+
+def _eo32(expert_offsets: torch.Tensor) -> torch.Tensor:
+    return expert_offsets if expert_offsets.dtype == torch.int32 else expert_offsets.to(torch.int32)
+
+
+def quantize_scales_for_hybrid(scale: torch.Tensor, Q_max: int = 64,
+                               super_group_size: int | None = None):
+    """Two-level scale factorisation: F[r,g] = max(|s[r,g-block]|,1e-12)/Q_max,
+    Q = rint(s / F)."""
+    assert scale.ndim == 2, "scale must be a 2D tensor [X_blocks, K_blocks]"
+    assert scale.dtype == torch.float32, "scale must be float32"
+    rows, kb = scale.shape
+    if super_group_size is None:
+        super_group_size = kb
+    nsg = cdiv(kb, super_group_size)
+    scale = scale.contiguous()
+    Q = torch.empty(rows, kb, dtype=torch.int32, device=scale.device)
+    F = torch.empty(rows, nsg, dtype=torch.float32, device=scale.device)
+    with torch.cuda.device(scale.device):
+        call("i8moe_quantize_scales", scale.data_ptr(), rows, kb, Q_max, super_group_size,
+             Q.data_ptr(), F.data_ptr(), _stream(scale))
+    return Q, F
+
+
+def moe_kernel_quantize_input_int8_hybrid_grouped(A, block_k: int, q_max: int,
+                                                  super_group_size: int, expert_offsets,
+                                                  tile_m: int, scale_offsets=None):
+    """Grouped quant of an expert-contiguous [M, K] activation."""
+    assert A.ndim == 2 and A.is_contiguous()
+    assert A.dtype in _DT
+    assert expert_offsets.ndim == 1 and expert_offsets.is_cuda
+    assert block_k > 0 and tile_m > 0 and super_group_size > 0
+    M, K = A.shape
+    eo = _eo32(expert_offsets)
+    E = eo.numel() - 1
+    qA, Q, F = _outputs(M, K, E, tile_m, block_k, super_group_size, A.device)
+    so, ready = _so(scale_offsets, E, A.device)
+    with torch.cuda.device(A.device):
+        call("i8moe_quant_grouped", A.data_ptr(), _DT[A.dtype], M, K, eo.data_ptr(), E, tile_m,
+             block_k, q_max, super_group_size, qA.data_ptr(), Q.data_ptr(), F.data_ptr(),
+             so.data_ptr(), ready, _stream(A))
+    return qA, Q, F, so[:-1]
+
+
+def fused_permute_quant_int8_hybrid_grouped(hidden_states, permuted_idx, topk: int,
+                                            block_k: int, q_max: int, super_group_size: int,
+                                            expert_offsets, tile_m: int, scale_offsets=None):
+    """Gather hidden_states[permuted_idx // topk] and quantise in one pass."""
+    assert hidden_states.ndim == 2 and hidden_states.is_contiguous()
+    assert hidden_states.dtype in _DT
+    assert permuted_idx.ndim == 1 and permuted_idx.is_cuda
+    assert permuted_idx.dtype == torch.int32
+    assert expert_offsets.ndim == 1 and expert_offsets.is_cuda
+    assert topk > 0 and block_k > 0 and tile_m > 0 and super_group_size > 0
+    n_token, K = hidden_states.shape
+    M = permuted_idx.numel()
+    eo = _eo32(expert_offsets)
+    E = eo.numel() - 1
+    qA, Q, F = _outputs(M, K, E, tile_m, block_k, super_group_size, hidden_states.device)
+    so, ready = _so(scale_offsets, E, hidden_states.device)
+    with torch.cuda.device(hidden_states.device):
+        call("i8moe_quant_permute", hidden_states.data_ptr(), _DT[hidden_states.dtype], n_token,
+             K, permuted_idx.data_ptr(), M, topk, eo.data_ptr(), E, tile_m, block_k, q_max,
+             super_group_size, qA.data_ptr(), Q.data_ptr(), F.data_ptr(), so.data_ptr(), ready,
+             _stream(hidden_states))
+    return qA, Q, F, so[:-1]
+
+
+def fused_silu_quant_int8_hybrid_grouped(mm1_out, block_k: int, q_max: int,
+                                         super_group_size: int, expert_offsets, tile_m: int,
+                                         scale_offsets=None):
+    """silu(gate) * up of the w13 output, quantised over the intermediate dim."""
+    assert mm1_out.ndim == 2 and mm1_out.is_contiguous()
+    assert mm1_out.dtype in _DT
+    assert expert_offsets.ndim == 1 and expert_offsets.is_cuda
+    assert block_k > 0 and tile_m > 0 and super_group_size > 0
+    sum_m, two_n = mm1_out.shape
+    assert two_n % 2 == 0, "w13 output must have an even last dim (2*N)"
+    N = two_n // 2
+    eo = _eo32(expert_offsets)
+    E = eo.numel() - 1
+    qA, Q, F = _outputs(sum_m, N, E, tile_m, block_k, super_group_size, mm1_out.device)
+    so, ready = _so(scale_offsets, E, mm1_out.device)
+    with torch.cuda.device(mm1_out.device):
+        call("i8moe_quant_silu", mm1_out.data_ptr(), _DT[mm1_out.dtype], sum_m, N,
+             eo.data_ptr(), E, tile_m, block_k, q_max, super_group_size, qA.data_ptr(),
+             Q.data_ptr(), F.data_ptr(), so.data_ptr(), ready, _stream(mm1_out))
+    return qA, Q, F, so[:-1]
+
+
+def _so(scale_offsets, E: int, device):
+    """Scale-offset buffer [E+1]; ``scale_offsets`` (already computed for the
+    same expert offsets and tile_m) is reused as is."""
+    if scale_offsets is not None:
+        assert scale_offsets.dtype == torch.int32 and scale_offsets.numel() == E + 1
+        return scale_offsets, 1
+    return torch.empty(E + 1, dtype=torch.int32, device=device), 0

@@ -1,0 +1,458 @@
+"""Parity of the sm_100a kernels (through the C ABI / torch ops) with the CPU
+oracle and with the golden vectors of the reference's own code.
+
+Tolerances:
+  * bit-exact: routing maps and offsets, int8 activations, Q/F scales, scale
+    offsets, the raw int32 GEMM accumulators, GEMM bf16/fp16 outputs,
+    per-tensor GEMM outputs;
+  * SiLU-dependent values (silu_and_mul, the a2 int8 activations): the
+    device expf and the host exp may differ by one float32 ulp, which can flip
+    one bf16 rounding; such flips must be rare (counted and bounded) and at
+    most one step;
+  * unpermute: the oracle emulates fp32 FMA in float64 (double rounding can
+    differ by one float32 ulp), so one bf16/fp16 ulp on a tiny fraction;
+  * final MoE output: max|y - ref| / max|ref| <= 1e-2.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ref_cpu as ref
+from tests.conftest import GOLDEN
+from tests.helpers import load_workloads
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+TDT = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
+
+
+@pytest.fixture(scope="module")
+def m():
+    import int8blockwisegemm_b200 as pkg
+    from int8blockwisegemm_b200 import _lib
+    _lib.device_error(0, clear=True)
+    yield pkg
+    assert _lib.device_error(0) == 0, "a kernel reported a device-side error"
+
+
+def npf(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu()
+    if t.is_floating_point():
+        return t.float().numpy()
+    return t.numpy()
+
+
+def ulp_diff(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
+    """Distance in units of the storage dtype's last place."""
+    if dtype == "bf16":
+        ia = a.astype(np.float32).view(np.int32) >> 16
+        ib = b.astype(np.float32).view(np.int32) >> 16
+    elif dtype == "fp16":
+        ia = a.astype(np.float16).view(np.int16).astype(np.int32)
+        ib = b.astype(np.float16).view(np.int16).astype(np.int32)
+    else:
+        ia = a.astype(np.float32).view(np.int32)
+        ib = b.astype(np.float32).view(np.int32)
+    ia = np.where(ia < 0, np.int32(-0x80000000) - ia, ia) if dtype == "fp32" else ia
+    return np.abs(ia.astype(np.int64) - ib.astype(np.int64))
+
+
+def inputs(name, seed=None):
+    wl = load_workloads()
+    cfg = wl.CONFIGS[name]
+    return cfg, wl.make_inputs(cfg, seed)
+
+
+# ---------------------------------------------------------------------------
+# routing
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name,ep", [("tiny", None), ("ragged", None), ("mid", None),
+                                     ("default", None), ("tiny", (1, 2)), ("default", (3, 8))])
+def test_routing_bit_exact(m, name, ep):
+    cfg, inp = inputs(name)
+    ids = inp["topk_ids"]
+    E = cfg.E
+    emap = None
+    n_local = E
+    if ep is not None:
+        r, size = ep
+        per = E // size
+        emap = torch.full((E,), -1, dtype=torch.int32)
+        emap[r * per:(r + 1) * per] = torch.arange(per, dtype=torch.int32)
+        n_local = per
+    hidden = inp["hidden"].to(DEV)
+    eft, inv, pidx = m.permute.moe_permute_metadata(
+        hidden, ids.to(DEV), E, n_local, None if emap is None else emap.to(DEV))
+    T, k = ids.shape
+    o_eft, o_inv, o_pidx = ref.moe_permute_metadata(
+        ids.numpy(), np.arange(T * k, dtype=np.int32), None if emap is None else emap.numpy(),
+        E, n_local, k)
+    np.testing.assert_array_equal(npf(eft), o_eft)
+    np.testing.assert_array_equal(npf(inv), o_inv.reshape(-1))
+    np.testing.assert_array_equal(npf(pidx), o_pidx)
+
+
+def test_route_for_gemm_extras(m):
+    cfg, inp = inputs("mid")
+    ids = inp["topk_ids"].to(DEV)
+    for tm in (64, 128):
+        eft, inv, pidx, eo, ps1, ps2, so = m.permute.moe_route_for_gemm(
+            ids, cfg.T, cfg.E, cfg.E, None, 2 * cfg.N, cfg.K, cfg.K, cfg.N, tm)
+        e = npf(eft)
+        np.testing.assert_array_equal(npf(eo), e)
+        cnt = e[1:] - e[:-1]
+        np.testing.assert_array_equal(npf(ps1), np.stack([cnt, np.full_like(cnt, 2 * cfg.N),
+                                                          np.full_like(cnt, cfg.K)], 1))
+        np.testing.assert_array_equal(npf(ps2), np.stack([cnt, np.full_like(cnt, cfg.K),
+                                                          np.full_like(cnt, cfg.N)], 1))
+        np.testing.assert_array_equal(npf(so), ref.scale_offsets_from(e, tm))
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16", "fp32"])
+def test_moe_permute_rows(m, dtype):
+    cfg, inp = inputs("ragged")
+    hidden = inp["hidden"].float().to(TDT[dtype]).to(DEV)
+    ids = inp["topk_ids"].to(DEV)
+    out, _, eft, inv, pidx = m.permute.moe_permute(hidden, None, ids, cfg.E)
+    src = npf(pidx).astype(np.int64) // cfg.topk
+    np.testing.assert_array_equal(npf(out), npf(hidden)[src])
+
+
+# ---------------------------------------------------------------------------
+# quantisation against the reference's Triton kernels (golden) and the oracle
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name", ["gq_fp32_tm64", "gq_fp16_tm128", "gq_bf16_tm64_ktail"])
+def test_grouped_quant_golden(m, name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    A = torch.from_numpy(g["A"]).to(TDT[str(g["dtype"])]).to(DEV)
+    eo = torch.from_numpy(g["eo"]).to(DEV)
+    qA, Q, F, so = m.quant.moe_kernel_quantize_input_int8_hybrid_grouped(
+        A, 128, 16, 2, eo, int(g["tile_m"]))
+    rows = g["Q"].shape[0]
+    lo, hi = int(g["eo"][0]), int(g["eo"][-1])
+    np.testing.assert_array_equal(npf(qA)[lo:hi], g["qA"][lo:hi])
+    np.testing.assert_array_equal(npf(Q)[:rows], g["Q"])
+    np.testing.assert_array_equal(npf(F)[:rows], g["F"])
+    np.testing.assert_array_equal(npf(so), g["so"])
+
+
+@pytest.mark.parametrize("name", ["sq_fp16_tm64", "sq_bf16_tm128"])
+def test_silu_quant_golden(m, name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    X = torch.from_numpy(g["X"]).to(TDT[str(g["dtype"])]).to(DEV)
+    eo = torch.from_numpy(g["eo"]).to(DEV)
+    qA, Q, F, so = m.quant.fused_silu_quant_int8_hybrid_grouped(X, 128, 16, 256, eo,
+                                                                int(g["tile_m"]))
+    rows = g["Q"].shape[0]
+    diff = np.abs(npf(qA).astype(np.int32) - g["qA"].astype(np.int32))
+    assert diff.max() <= 1 and (diff > 0).mean() < 1e-3, (diff.max(), (diff > 0).sum())
+    np.testing.assert_array_equal(npf(so), g["so"])
+    # scales can only move if a flipped element was a tile's absmax
+    assert (npf(F)[:rows] != g["F"]).mean() < 0.05
+
+
+def test_quantize_scales_golden(m):
+    g = dict(np.load(GOLDEN / "scales_sg3.npz"))
+    Q, F = m.quant.quantize_scales_for_hybrid(torch.from_numpy(g["s"]).to(DEV), 16, 3)
+    np.testing.assert_array_equal(npf(Q), g["Q"])
+    np.testing.assert_array_equal(npf(F), g["F"])
+
+
+@pytest.mark.parametrize("name,dtype,tm", [("mid", "bf16", 128), ("mid", "fp16", 64),
+                                           ("mid", "fp32", 128), ("ragged", "bf16", 64),
+                                           ("default", "bf16", 128)])
+def test_permute_quant_vs_oracle(m, name, dtype, tm):
+    cfg, inp = inputs(name)
+    hidden = inp["hidden"].float().to(TDT[dtype]).to(DEV)
+    eft, inv, pidx = m.permute.moe_permute_metadata(hidden, inp["topk_ids"].to(DEV), cfg.E)
+    eo = eft.to(torch.int32)
+    qA, Q, F, so = m.quant.fused_permute_quant_int8_hybrid_grouped(hidden, pidx, cfg.topk, 128,
+                                                                   16, cfg.sg, eo, tm)
+    o_q, o_s, o_so = ref.fused_permute_quant(npf(hidden), npf(pidx), cfg.topk, npf(eo), tm)
+    o_Q, o_F = ref.quantize_scales_for_hybrid(o_s, 16, cfg.sg)
+    rows = o_Q.shape[0]
+    np.testing.assert_array_equal(npf(qA), o_q)
+    np.testing.assert_array_equal(npf(Q)[:rows], o_Q)
+    np.testing.assert_array_equal(npf(F)[:rows], o_F)
+    np.testing.assert_array_equal(npf(so), o_so[:-1])
+
+
+# ---------------------------------------------------------------------------
+# GEMMs
+# ---------------------------------------------------------------------------
+
+def _gemm_case(seed, counts, N, K, qbs=128, sg=256, tm=128):
+    g = torch.Generator().manual_seed(seed)
+    E = len(counts)
+    M = int(sum(counts))
+    eo = torch.tensor([0, *np.cumsum(counts).tolist()], dtype=torch.int32)
+    ps = torch.stack([torch.tensor(counts, dtype=torch.int32), torch.full((E,), N, dtype=torch.int32),
+                      torch.full((E,), K, dtype=torch.int32)], 1).contiguous()
+    nqb = -(-K // qbs)
+    nsg = -(-nqb // sg)
+    nsb = -(-N // 64)
+    rows = int(sum(-(-c // tm) for c in counts)) + 1
+    A = torch.randint(-128, 128, (M, K), generator=g, dtype=torch.int8)
+    B = torch.randint(-128, 128, (E, N, K), generator=g, dtype=torch.int8)
+    QA = torch.randint(0, 17, (rows, nqb), generator=g, dtype=torch.int32)
+    FA = torch.empty(rows, nsg).log_normal_(-6, 0.5, generator=g)
+    QB = torch.randint(0, 17, (E, nsb, nqb), generator=g, dtype=torch.int32)
+    FB = torch.empty(E, nsb, nsg).log_normal_(-6, 0.5, generator=g)
+    so = torch.from_numpy(ref.scale_offsets_from(eo.numpy(), tm)[:-1].astype(np.int32))
+    return dict(A=A, B=B, QA=QA, FA=FA, QB=QB, FB=FB, eo=eo, ps=ps, so=so, qbs=qbs, sg=sg, tm=tm,
+                N=N, K=K, E=E, M=M)
+
+
+GEMM_CASES = [
+    dict(seed=1, counts=[300, 0, 17, 128, 1], N=256, K=256),
+    dict(seed=2, counts=[5, 70, 0, 64, 129], N=192, K=160, tm=64),       # K residue, N tail
+    dict(seed=3, counts=[200, 33], N=136, K=384, qbs=256),               # 2 K-tiles per block
+    dict(seed=4, counts=[0, 0, 257], N=512, K=2048, sg=8),
+    dict(seed=5, counts=[1], N=64, K=32, tm=64),                          # single tiny problem
+]
+
+
+@pytest.mark.parametrize("case", GEMM_CASES, ids=lambda c: f"s{c['seed']}")
+def test_hybrid_gemm_bit_exact(m, case):
+    c = _gemm_case(**case)
+    d = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in c.items()}
+    fn = (m.ops.cutlass_int8_blockwise_hybrid_grouped if c["tm"] == 128
+          else m.ops.cutlass_int8_blockwise_hybrid_grouped_small)
+    o_out, o_w = ref.hybrid_grouped_gemm(c["A"].numpy(), c["QA"].numpy(), c["FA"].numpy(),
+                                         c["B"].numpy(), c["QB"].numpy(), c["FB"].numpy(),
+                                         c["eo"].numpy(), c["ps"].numpy(), c["qbs"], c["tm"],
+                                         scale_offsets=c["so"].numpy(), return_w=True)
+    acc = torch.zeros(c["M"], c["N"], dtype=torch.int32, device=DEV)
+    fn(d["A"], d["QA"], d["FA"], d["B"], d["QB"], d["FB"], d["eo"], d["ps"], acc, c["qbs"],
+       c["sg"], d["so"])
+    np.testing.assert_array_equal(npf(acc), o_w)
+    for odt, name in ((torch.bfloat16, "bf16"), (torch.float16, "fp16")):
+        out = torch.zeros(c["M"], c["N"], dtype=odt, device=DEV)
+        fn(d["A"], d["QA"], d["FA"], d["B"], d["QB"], d["FB"], d["eo"], d["ps"], out, c["qbs"],
+           c["sg"], None)   # scale_offsets derived in-kernel from problem_sizes
+        exp = o_out if name == "bf16" else ref.hybrid_grouped_gemm(
+            c["A"].numpy(), c["QA"].numpy(), c["FA"].numpy(), c["B"].numpy(), c["QB"].numpy(),
+            c["FB"].numpy(), c["eo"].numpy(), c["ps"].numpy(), c["qbs"], c["tm"],
+            out_dtype="fp16")
+        np.testing.assert_array_equal(npf(out), exp)
+
+
+def test_hybrid_gemm_bias(m):
+    c = _gemm_case(seed=7, counts=[100, 0, 60], N=192, K=256)
+    d = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in c.items()}
+    g = torch.Generator().manual_seed(9)
+    for bias in (torch.randn(c["N"], generator=g), torch.randn(c["E"], c["N"], generator=g)):
+        out = torch.zeros(c["M"], c["N"], dtype=torch.bfloat16, device=DEV)
+        m.ops.cutlass_int8_blockwise_hybrid_grouped_bias(
+            d["A"], d["QA"], d["FA"], d["B"], d["QB"], d["FB"], d["eo"], d["ps"], out,
+            bias.to(DEV), c["qbs"], c["sg"], d["so"])
+        exp = ref.hybrid_grouped_gemm(c["A"].numpy(), c["QA"].numpy(), c["FA"].numpy(),
+                                      c["B"].numpy(), c["QB"].numpy(), c["FB"].numpy(),
+                                      c["eo"].numpy(), c["ps"].numpy(), c["qbs"], c["tm"],
+                                      scale_offsets=c["so"].numpy(), bias=bias.numpy())
+        assert ulp_diff(npf(out), exp, "bf16").max() <= 1
+
+
+def test_per_tensor_grouped_mm(m):
+    c = _gemm_case(seed=11, counts=[64, 0, 190, 3], N=256, K=512)
+    d = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in c.items()}
+    out = torch.zeros(c["M"], c["N"], dtype=torch.bfloat16, device=DEV)
+    m.ops.cutlass_int8_grouped_mm(d["A"], d["B"], out, 0.0123, 0.0456, d["eo"], d["ps"])
+    exp = ref.int8_grouped_mm(c["A"].numpy(), c["B"].numpy(), 0.0123, 0.0456, c["eo"].numpy(),
+                              c["ps"].numpy())
+    np.testing.assert_array_equal(npf(out), exp)
+    g = torch.Generator().manual_seed(12)
+    a_s = torch.rand(c["M"], generator=g) * 0.01
+    b_s = torch.empty(c["E"]).log_normal_(-6, 0.5, generator=g)
+    m.ops.int8_grouped_mm_scaled(d["A"], d["B"], out, a_s.to(DEV), b_s.to(DEV), d["eo"], d["ps"])
+    exp = ref.int8_grouped_mm(c["A"].numpy(), c["B"].numpy(), 1.0, 1.0, c["eo"].numpy(),
+                              c["ps"].numpy(), a_row_scale=a_s.numpy(),
+                              b_expert_scale=b_s.numpy())
+    np.testing.assert_array_equal(npf(out), exp)
+    bad = d["ps"].clone()
+    bad[0, 0] += 1
+    with pytest.raises(RuntimeError, match="problem_sizes"):
+        m.ops.cutlass_int8_grouped_mm(d["A"], d["B"], out, 1.0, 1.0, d["eo"], bad)
+
+
+def test_gemm_input_checks(m):
+    c = _gemm_case(seed=1, counts=[10], N=64, K=128)
+    d = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in c.items()}
+    out = torch.zeros(c["M"], c["N"], dtype=torch.float32, device=DEV)
+    with pytest.raises(RuntimeError, match="out must be bfloat16"):
+        m.ops.cutlass_int8_blockwise_hybrid_grouped(d["A"], d["QA"], d["FA"], d["B"], d["QB"],
+                                                    d["FB"], d["eo"], d["ps"], out, 128, 256)
+    out = torch.zeros(c["M"], c["N"], dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(RuntimeError, match="quant_block_size"):
+        m.ops.cutlass_int8_blockwise_hybrid_grouped(d["A"], d["QA"], d["FA"], d["B"], d["QB"],
+                                                    d["FB"], d["eo"], d["ps"], out, 64, 256)
+
+
+# ---------------------------------------------------------------------------
+# activation / unpermute
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16", "fp32"])
+def test_silu_and_mul(m, dtype):
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(333, 2 * 256, generator=g) * 4).to(TDT[dtype]).to(DEV)
+    out = torch.empty(333, 256, dtype=TDT[dtype], device=DEV)
+    m.ops.silu_and_mul(out, x)
+    exp = ref.silu_and_mul(npf(x), dtype)
+    ud = ulp_diff(npf(out), exp, dtype)
+    assert ud.max() <= 1 and (ud > 0).mean() < 1e-3
+
+
+@pytest.mark.parametrize("dtype,ep", [("bf16", False), ("fp16", False), ("fp32", False),
+                                      ("bf16", True)])
+def test_unpermute(m, dtype, ep):
+    cfg, inp = inputs("mid")
+    T, k = inp["topk_ids"].shape
+    R = T * k
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(R, cfg.K, generator=g).to(TDT[dtype]).to(DEV)
+    perm = torch.randperm(R, generator=g).to(torch.int32)
+    eft = torch.tensor([0, R - 100 if ep else R], dtype=torch.int64)
+    out = torch.empty(T, cfg.K, dtype=TDT[dtype], device=DEV)
+    m.ops.moe_unpermute(x, inp["topk_weights"].to(DEV), perm.to(DEV), eft.to(DEV), k, out)
+    exp = ref.moe_unpermute(npf(x), inp["topk_weights"].numpy(), perm.numpy(), eft.numpy(), k,
+                            dtype)
+    ud = ulp_diff(npf(out), exp, dtype)
+    assert ud.max() <= 1 and (ud > 0).mean() < 1e-3
+
+
+# ---------------------------------------------------------------------------
+# full forward
+# ---------------------------------------------------------------------------
+
+def run_forward(m, cfg, inp, fuse_permute=True, fuse_silu=True, expert_map=None, rank_slice=None,
+                trace=None, graph=False):
+    r = m.cutlass_runner
+    r._USE_FUSED_PERMUTE_QUANT_W1 = fuse_permute
+    r._USE_FUSED_SILU_QUANT_W2 = fuse_silu
+    dt = TDT[cfg.dtype]
+    w = {k: inp[k] for k in ("w13", "w2", "w13_q", "w13_f", "w2_q", "w2_f")}
+    if rank_slice is not None:
+        w = {k: v[rank_slice].contiguous() for k, v in w.items()}
+    w = {k: v.to(DEV) for k, v in w.items()}
+    T, k = inp["topk_ids"].shape
+    R = T * k
+    K, N = cfg.K, cfg.N
+    ws13 = torch.empty(R, max(2 * N, K), dtype=dt, device=DEV)
+    ws2 = torch.empty(R, max(N, K), dtype=dt, device=DEV)
+    out = torch.empty(T, K, dtype=dt, device=DEV)
+    args = dict(output=out, hidden_states=inp["hidden"].to(DEV), w1=w["w13"], w2=w["w2"],
+                topk_ids=inp["topk_ids"].to(DEV), topk_weights=inp["topk_weights"].to(DEV),
+                activation=m.activation.MoEActivation.SILU, global_num_experts=cfg.E,
+                expert_map=None if expert_map is None else expert_map.to(DEV),
+                w1_qscale=w["w13_q"], w1_fscale=w["w13_f"], w2_qscale=w["w2_q"],
+                w2_fscale=w["w2_f"], workspace13=ws13, workspace2=ws2,
+                quant_block_size=cfg.quant_block, super_group_size=cfg.sg, q_max=cfg.q_max)
+    if graph:
+        r._run_cutlass_int8_hybrid_grouped_moe(**args)   # warm-up (allocator, attributes)
+        torch.cuda.synchronize()
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            r._run_cutlass_int8_hybrid_grouped_moe(**args)
+        out.zero_()
+        gph.replay()
+        torch.cuda.synchronize()
+        return out
+    r._run_cutlass_int8_hybrid_grouped_moe(**args, _trace=trace)
+    torch.cuda.synchronize()
+    return out
+
+
+FWD_GOLDEN = [("fwd_tiny", "tiny", True, True, None), ("fwd_tiny_unfused", "tiny", False, False, None),
+              ("fwd_ragged", "ragged", True, True, None), ("fwd_tm128", "tm128", True, True, None),
+              ("fwd_tiny_ep1of2", "tiny", True, True, (1, 2))]
+
+
+@pytest.mark.parametrize("gname,cname,fp,fs,ep", FWD_GOLDEN, ids=[f[0] for f in FWD_GOLDEN])
+def test_forward_against_reference_golden(m, gname, cname, fp, fs, ep):
+    g = dict(np.load(GOLDEN / f"{gname}.npz"))
+    cfg, inp = inputs(cname)
+    emap, sl = None, None
+    if ep is not None:
+        emap = torch.from_numpy(g["expert_map"])
+        loc = np.nonzero(g["expert_map"] >= 0)[0]
+        sl = slice(int(loc[0]), int(loc[-1]) + 1)
+    tr = {}
+    out = run_forward(m, cfg, inp, fp, fs, emap, sl, trace=tr)
+    v = int(g["valid"])
+    rows = g["a1_Q"].shape[0]
+    assert tr["tile_m"] == int(g["tile_m"])
+    np.testing.assert_array_equal(npf(tr["eft"]), g["eft"])
+    np.testing.assert_array_equal(npf(tr["inv"]), g["inv"].reshape(-1))
+    if "pidx" in tr:
+        np.testing.assert_array_equal(npf(tr["pidx"]), g["pidx"])
+    np.testing.assert_array_equal(npf(tr["a1q"])[:v], g["a1q"])
+    np.testing.assert_array_equal(npf(tr["a1_Q"])[:rows], g["a1_Q"])
+    np.testing.assert_array_equal(npf(tr["a1_F"])[:rows], g["a1_F"])
+    np.testing.assert_array_equal(npf(tr["a1_so"]), g["a1_so"])
+    np.testing.assert_array_equal(npf(tr["mm1"])[:v], g["mm1"])
+    d2 = np.abs(npf(tr["a2q"])[:v].astype(np.int32) - g["a2q"].astype(np.int32))
+    assert d2.max() <= 1 and (d2 > 0).mean() < 1e-3
+    o = npf(out)
+    assert np.abs(o - g["out"]).max() / np.abs(g["out"]).max() <= 1e-2
+
+
+def test_forward_cuda_graph_replay(m):
+    cfg, inp = inputs("mid")
+    eager = run_forward(m, cfg, inp).clone()
+    replay = run_forward(m, cfg, inp, graph=True)
+    assert torch.equal(eager, replay)
+
+
+def test_forward_default_config_stagewise(m):
+    """BASELINE configs[1] at full size.  Every stage is checked against the
+    oracle applied to the device's own previous-stage output (GEMMs on a sample
+    of experts), plus the end-to-end output tolerance on sampled tokens."""
+    cfg, inp = inputs("default")
+    tr = {}
+    out = run_forward(m, cfg, inp, True, True, trace=tr)
+    T, k = inp["topk_ids"].shape
+    R = T * k
+    eft = npf(tr["eft"])
+    o_eft, o_inv, o_pidx = ref.moe_permute_metadata(
+        inp["topk_ids"].numpy(), np.arange(R, dtype=np.int32), None, cfg.E, cfg.E, k)
+    np.testing.assert_array_equal(eft, o_eft)
+    np.testing.assert_array_equal(npf(tr["inv"]), o_inv.reshape(-1))
+    tm = tr["tile_m"]
+    assert tm == 128
+    a1q, s1, so1 = ref.fused_permute_quant(npf(inp["hidden"]), o_pidx, k, eft, tm)
+    Q1, F1 = ref.quantize_scales_for_hybrid(s1, cfg.q_max, cfg.sg)
+    np.testing.assert_array_equal(npf(tr["a1q"]), a1q)
+    np.testing.assert_array_equal(npf(tr["a1_Q"])[:Q1.shape[0]], Q1)
+    np.testing.assert_array_equal(npf(tr["a1_F"])[:F1.shape[0]], F1)
+    # GEMMs on a sample of experts (inputs: the device's own int8 activations)
+    sample = [0, 1, 77, 128, 255]
+    for e in sample:
+        lo, hi = int(eft[e]), int(eft[e + 1])
+        cnt = hi - lo
+        ps = np.array([[cnt, 2 * cfg.N, cfg.K]])
+        s0 = int(so1[e])
+        mm1 = ref.hybrid_grouped_gemm(npf(tr["a1q"])[lo:hi], npf(tr["a1_Q"])[s0:], npf(tr["a1_F"])[s0:],
+                                      inp["w13"][e:e + 1].numpy(), inp["w13_q"][e:e + 1].numpy(),
+                                      inp["w13_f"][e:e + 1].numpy(), np.array([0, cnt]), ps, 128,
+                                      tm, scale_offsets=np.array([0]))
+        np.testing.assert_array_equal(npf(tr["mm1"])[lo:hi], mm1)
+        ps2 = np.array([[cnt, cfg.K, cfg.N]])
+        mm2 = ref.hybrid_grouped_gemm(npf(tr["a2q"])[lo:hi], npf(tr["a2_Q"])[s0:], npf(tr["a2_F"])[s0:],
+                                      inp["w2"][e:e + 1].numpy(), inp["w2_q"][e:e + 1].numpy(),
+                                      inp["w2_f"][e:e + 1].numpy(), np.array([0, cnt]), ps2, 128,
+                                      tm, scale_offsets=np.array([0]))
+        np.testing.assert_array_equal(npf(tr["mm2"])[lo:hi], mm2)
+    # SiLU + requant on the device's own mm1
+    a2q, s2, _ = ref.fused_silu_quant(npf(tr["mm1"]), eft, tm, "bf16")
+    d2 = np.abs(npf(tr["a2q"]).astype(np.int32) - a2q.astype(np.int32))
+    assert d2.max() <= 1 and (d2 > 0).mean() < 1e-4
+    # unpermute on the device's own mm2
+    o = ref.moe_unpermute(npf(tr["mm2"]), inp["topk_weights"].numpy(), o_inv.reshape(-1), eft, k,
+                          "bf16")
+    ud = ulp_diff(npf(out), o, "bf16")
+    assert ud.max() <= 1 and (ud > 0).mean() < 1e-3
