@@ -30,9 +30,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import threading
 import time
 from pathlib import Path
@@ -82,60 +80,69 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """SM clock and clock-event (throttle) reasons polled through NVML every
+    ~5 ms in a background thread while the timed region runs (read-only
+    queries; no GPU setting is touched)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._h = None
+
+    def _handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        try:
+            p = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+
+    def _run(self):
+        nv = self._nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                rs = get_reasons(self._h)
+                self.samples.append((sm, rs))
+            except Exception:
+                pass
+            time.sleep(0.005)
 
     def __enter__(self):
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
-                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            self._h = self._handle()
+            self.max_mhz = self._nvml.nvmlDeviceGetMaxClockInfo(self._h, self._nvml.NVML_CLOCK_SM)
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if not self.path or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        rows = []
-        for line in Path(self.path).read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append(parts)
-            except Exception:
-                pass
-        os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        load = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
-        return {"sm_mhz": statistics.median(load) if load else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+        sm = [s for s, _ in self.samples]
+        reasons = sorted({name for _, r in self.samples for bit, name in self.REASONS.items()
+                          if r & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "sm_mhz_min": min(sm)}
 
 
 def dist_setup(args):
@@ -258,9 +265,11 @@ def time_w13_gemm(pkg, cfg, st, tr, iters=20):
     tm = tr["tile_m"]
     fn = (pkg.ops.cutlass_int8_blockwise_hybrid_grouped if tm == 128
           else pkg.ops.cutlass_int8_blockwise_hybrid_grouped_small)
+    R = tr["a1q"].shape[0]
+    out = st["workspace13"].flatten()[: R * 2 * cfg.N].view(R, 2 * cfg.N)
     args = (tr["a1q"], tr["a1_Q"], tr["a1_F"], st["w1"], st["w1_qscale"], st["w1_fscale"],
-            tr["expert_offsets"], tr["problem_sizes1"], st["workspace13"][: tr["a1q"].shape[0] *
-            2 * cfg.N].view(-1, 2 * cfg.N), cfg.quant_block, cfg.sg, tr["a1_so"])
+            tr["expert_offsets"], tr["problem_sizes1"], out, cfg.quant_block, cfg.sg,
+            tr["a1_so"])
     for _ in range(3):
         fn(*args)
     s = torch.cuda.current_stream()

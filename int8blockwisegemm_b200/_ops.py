@@ -137,10 +137,13 @@ def _check_hybrid(a_q, a_qs, a_fs, b_q, b_qs, b_fs, eo, ps, out):
 
 def _hybrid(tile_m: int, with_bias: bool):
     def impl(a_q, a_qs, a_fs, b_q, b_qs, b_fs, eo, ps, out, *rest):
+        # the dispatcher passes trailing defaulted arguments only when given
         if with_bias:
-            bias, qbs, sg, so = rest
+            bias, qbs, sg = rest[:3]
+            so = rest[3] if len(rest) > 3 else None
         else:
-            qbs, sg, so = rest
+            qbs, sg = rest[:2]
+            so = rest[2] if len(rest) > 2 else None
             bias = None
         _check_hybrid(a_q, a_qs, a_fs, b_q, b_qs, b_fs, eo, ps, out)
         E, N, K = b_q.shape

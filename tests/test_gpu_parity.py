@@ -45,18 +45,23 @@ def npf(t: torch.Tensor) -> np.ndarray:
 
 
 def ulp_diff(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
-    """Distance in units of the storage dtype's last place."""
-    if dtype == "bf16":
-        ia = a.astype(np.float32).view(np.int32) >> 16
-        ib = b.astype(np.float32).view(np.int32) >> 16
-    elif dtype == "fp16":
-        ia = a.astype(np.float16).view(np.int16).astype(np.int32)
-        ib = b.astype(np.float16).view(np.int16).astype(np.int32)
-    else:
-        ia = a.astype(np.float32).view(np.int32)
-        ib = b.astype(np.float32).view(np.int32)
-    ia = np.where(ia < 0, np.int32(-0x80000000) - ia, ia) if dtype == "fp32" else ia
-    return np.abs(ia.astype(np.int64) - ib.astype(np.int64))
+    """Distance in units of the storage dtype's last place (sign-magnitude
+    bit patterns mapped to a monotone integer line)."""
+    def ordered(x):
+        if dtype == "bf16":
+            i = (x.astype(np.float32).view(np.int32) >> 16).astype(np.int64)
+            sign = i & 0x8000
+            mag = i & 0x7FFF
+        elif dtype == "fp16":
+            i = x.astype(np.float16).view(np.uint16).astype(np.int64)
+            sign = i & 0x8000
+            mag = i & 0x7FFF
+        else:
+            i = x.astype(np.float32).view(np.uint32).astype(np.int64)
+            sign = i & 0x80000000
+            mag = i & 0x7FFFFFFF
+        return np.where(sign != 0, -mag, mag)
+    return np.abs(ordered(a) - ordered(b))
 
 
 def inputs(name, seed=None):
