@@ -11,22 +11,23 @@
 //     out = dtype(float(sum_k a*b) * alpha) with alpha per tensor, or
 //     per-token x per-expert (extension).
 //
-// Structure (one CTA per SM, 10 warps):
+// Structure (one CTA per SM, 10 warps; tiles of 128 rows x 256 columns):
 //   warp 0      TMA producer: A tile [128 rows x 128 K] and B tile
 //               [BN x 128 K] per K-tile, 128-byte swizzle, into a STAGES-deep
 //               shared-memory ring guarded by full/empty mbarriers.
 //   warp 1      TMEM allocator + single-thread MMA issuer:
-//               tcgen05.mma.cta_group::1.kind::i8, M=128, N=BN, K=32, four per
-//               K-tile, accumulating one quant block into one of NACC TMEM
-//               accumulator buffers (BN columns each); tcgen05.commit frees
+//               tcgen05.mma.cta_group::1.kind::i8, M=128, N=256, K=32, four
+//               per K-tile, accumulating one quant block into one of two TMEM
+//               accumulator buffers (256 columns each); tcgen05.commit frees
 //               the smem stage and, at the end of a quant block, signals the
 //               epilogue.
 //   warps 2..9  epilogue: TMEM lane quadrant = warp % 4, column half =
-//               (warp - 2) / 4.  Each thread owns one output row and 64
-//               columns: tcgen05.ld the block partial, W += q * P (int32
-//               IMAD), release the TMEM buffer; after the last block convert,
-//               scale, round, stage the row in shared memory and store it
-//               with one bulk copy (rows beyond the expert are not stored, so
+//               (warp - 2) / 4.  Each thread owns one output row and 128
+//               columns: tcgen05.ld the block partial in 8-column chunks
+//               (the next chunk's load overlaps this chunk's accumulation),
+//               release the TMEM buffer, W += q * P (int32 IMAD); after the
+//               last block convert, scale, round and store the row with 16-B
+//               stores (rows beyond the expert are not stored, so
 //               neighbouring experts are never overwritten).
 // Tiles: (expert, 128-row m-tile, BN-col n-tile), m-tile major, walked
 // round-robin by the persistent CTAs; the per-expert m-tile prefix is built
@@ -38,6 +39,7 @@
 // with pad = 128*ceil(K/128) - K; the TMA load of tile 0 starts at the
 // negative column -pad and the out-of-range columns are zero-filled.
 #include <algorithm>
+#include <cstdlib>
 #include <cudaTypedefs.h>
 #include <type_traits>
 #include <mutex>
@@ -62,16 +64,15 @@ int read_gemm_error(uint32_t* w, int clear) {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BN = 256;
 constexpr int BK = 128;  // bytes == int8 elements per K-tile
-constexpr int STAGES = 5;
-constexpr int NACC = 4;
-constexpr int kThreads = 320;
+constexpr int STAGES = 4;
+constexpr int NACC = 2;
 constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue warps
 constexpr int kMaxExperts = 1024;
 constexpr int kTileABytes = BM * BK;
 constexpr int kTileBBytes = BN * BK;
-constexpr int kStageRow = 2 * 128 + 16;  // staging row: 2 column halves x 128 B + pad
 constexpr uint32_t kTmemCols = NACC * BN;
 constexpr uint32_t kIdesc = idesc_i8(BM, BN);
 
@@ -96,13 +97,13 @@ struct GemmParams {
   int q_stride, f_stride, nsb;
   int tile_m;
   int n_tiles;
+  int prefetch;  // K-tiles prefetched into L2 ahead of the smem loads (0: off)
 };
 
 struct SmemLayout {
   static constexpr int kA = 0;
   static constexpr int kB = kA + STAGES * kTileABytes;
-  static constexpr int kOut = kB + STAGES * kTileBBytes;
-  static constexpr int kBar = kOut + BM * kStageRow;  // 8-B aligned
+  static constexpr int kBar = kB + STAGES * kTileBBytes;  // 8-B aligned
   static constexpr int kNumBars = 2 * STAGES + 2 * NACC + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;   // tmem base, abort flag
   static constexpr int kPrefix = kMisc + 16;          // mt_prefix[E+1], so_prefix[E+1]
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar_final = bar_acce + NACC * 8;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SmemLayout::kMisc);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SmemLayout::kMisc + 4);
-  int* s_tmp = reinterpret_cast<int*>(smem + SmemLayout::kOut);  // scratch before use
+  int* s_tmp = reinterpret_cast<int*>(smem + SmemLayout::kA);  // scratch before the first TMA
   int* mt_prefix = reinterpret_cast<int*>(smem + SmemLayout::kPrefix);
   int* so_prefix = mt_prefix + (p.E + 1);
 
@@ -246,9 +247,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
-        const int row0 = __ldg(p.eo + ti.e) + ti.mt * BM;
+      // With p.prefetch > 0, the K-tile p.prefetch steps ahead of the one
+      // being loaded into shared memory (possibly in the next tile) is
+      // prefetched into L2 so first touches of weight tiles in HBM overlap.
+      int t = blockIdx.x;
+      TileInfo ti = decode_tile(t < total_tiles ? t : 0, mt_prefix, p.E, p.n_tiles);
+      int row0 = __ldg(p.eo + ti.e) + ti.mt * BM;
+      int tn = t + gridDim.x;
+      TileInfo tin = decode_tile(tn < total_tiles ? tn : 0, mt_prefix, p.E, p.n_tiles);
+      int row0n = __ldg(p.eo + tin.e) + tin.mt * BM;
+      for (; t < total_tiles && ok; t += gridDim.x) {
         const int n0 = ti.nt * BN;
         for (int kt = 0; kt < p.kt_total; ++kt) {
           if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, s_abort, &g_err_gemm,
@@ -256,14 +264,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          const int kx = kt * BK - p.k_pad;
           const uint32_t fb = bar_full + 8 * stage;
           mbar_arrive_expect_tx(fb, kTileABytes + kTileBBytes);
-          const int kx = kt * BK - p.k_pad;
           tma_load_2d(sbase + SmemLayout::kA + stage * kTileABytes, &tmA, fb, kx, row0);
           tma_load_3d(sbase + SmemLayout::kB + stage * kTileBBytes, &tmB, fb, kx, n0, ti.e);
+          if (p.prefetch > 0) {
+            const int pk = kt + p.prefetch;
+            if (pk < p.kt_total) {
+              const int pkx = pk * BK - p.k_pad;
+              if (pkx >= 0) {
+                tma_prefetch_l2_3d(&tmB, pkx, n0, ti.e);
+                tma_prefetch_l2_2d(&tmA, pkx, row0);
+              }
+            } else if (tn < total_tiles && pk - p.kt_total < p.kt_total) {
+              const int pkx = (pk - p.kt_total) * BK - p.k_pad;
+              if (pkx >= 0) {
+                tma_prefetch_l2_3d(&tmB, pkx, tin.nt * BN, tin.e);
+                tma_prefetch_l2_2d(&tmA, pkx, row0n);
+              }
+            }
+          }
           issued[stage] = true;
           issued_phase[stage] = phase;
           if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+        ti = tin;
+        row0 = row0n;
+        tn += gridDim.x;
+        if (tn < total_tiles) {
+          tin = decode_tile(tn, mt_prefix, p.E, p.n_tiles);
+          row0n = __ldg(p.eo + tin.e) + tin.mt * BM;
         }
       }
       if (!ok) {
@@ -326,131 +357,137 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ================= epilogue =================
+    // ================= epilogue (8 warps) =================
+    // TMEM lane quadrant = warp % 4 (hardware rule), column half =
+    // (warp - 2) / 4: each thread owns one row and 128 columns (two 64-column
+    // weight-scale blocks) of the 128 x 256 tile.
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int rl = quad * 32 + lane;  // row within the tile == TMEM lane
-    const uint32_t t_lane = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* stage_row = smem + SmemLayout::kOut + rl * kStageRow + half * 128;
-    const uint32_t stage_row_s = smem_u32(stage_row);
+    const uint32_t t_col = (static_cast<uint32_t>(quad * 32) << 16) + half * 128;
     int acc = 0;
     uint32_t aphase = 0;
     bool ok = true;
-    bool pending_store = false;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
       const int m_e = __ldg(p.ps + 3 * ti.e);
       const int lrow = ti.mt * BM + rl;
       const bool row_ok = lrow < m_e;
-      const int col0 = ti.nt * BN + half * 64;
-      const bool col_ok = col0 < p.N;
+      const int col0 = ti.nt * BN + half * 128;
+      const bool c0_ok = col0 < p.N;
+      const bool c1_ok = col0 + 64 < p.N;
       const int so_e = p.so ? __ldg(p.so + ti.e) : so_prefix[ti.e];
       const int srow = so_e + (row_ok ? lrow : 0) / p.tile_m;
       const int jb = col0 / 64;
-      int32_t W[64];
+      const int32_t* qa_row = p.qa + static_cast<int64_t>(srow) * p.q_stride;
+      const int32_t* qb_col = p.qb + (static_cast<int64_t>(ti.e) * p.nsb + jb) * p.q_stride;
+      int q0 = 1, q1 = 1;  // Q_A * Q_B of the two 64-column blocks, current q-block
+      auto qfac = [&](int qb, int& r0, int& r1) {
+        if (MODE != kHybrid) { r0 = r1 = 1; return; }
+        const int qa = row_ok ? __ldg(qa_row + qb) : 0;
+        r0 = c0_ok ? qa * __ldg(qb_col + qb) : 0;
+        r1 = c1_ok ? qa * __ldg(qb_col + p.q_stride + qb) : 0;
+      };
+      int32_t W[128];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) W[i] = 0;
-      for (int qb = 0; qb < p.nq; ++qb) {
-        int q = 1;
-        if (MODE == kHybrid) {
-          const int qa = row_ok ? __ldg(p.qa + static_cast<int64_t>(srow) * p.q_stride + qb) : 0;
-          const int qbv =
-              col_ok ? __ldg(p.qb + (static_cast<int64_t>(ti.e) * p.nsb + jb) * p.q_stride + qb)
-                     : 0;
-          q = qa * qbv;
-        }
-        if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm, kErrEpilogueTimeout)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t P0[32], P1[32];
-        const uint32_t taddr = tmem_base + t_lane + acc * BN + half * 64;
-        tmem_ld32(taddr, P0);
-        tmem_ld32(taddr + 32, P1);
-        tmem_wait_ld();
-        if (MODE == kHybrid) {
+      for (int i = 0; i < 128; ++i) W[i] = 0;
+      // Pipelined at 8-column granularity: chunk c+1 (or the next block's
+      // chunk 0) is in flight while chunk c is accumulated; the accumulator
+      // buffer goes back to the MMA warp as soon as its last chunk landed.
+      uint32_t P0[8], P1[8];
+      qfac(0, q0, q1);
+      if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm, kErrEpilogueTimeout)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      tmem_ld8(tmem_base + t_col + acc * BN, P0);
+      for (int qb = 0; qb < p.nq && ok; ++qb) {
+        const int qa0 = q0, qa1 = q1;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            W[i] += q * static_cast<int32_t>(P0[i]);
-            W[32 + i] += q * static_cast<int32_t>(P1[i]);
+        for (int c = 0; c < 16; ++c) {
+          uint32_t(&cur)[8] = (c & 1) ? P1 : P0;
+          uint32_t(&nxt)[8] = (c & 1) ? P0 : P1;
+          tmem_wait_ld(cur);
+          if (c < 15) {
+            tmem_ld8(tmem_base + t_col + acc * BN + 8 * (c + 1), nxt);
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acce + 8 * acc);
+            if (++acc == NACC) acc = 0, aphase ^= 1;
+            if (qb + 1 < p.nq) {
+              qfac(qb + 1, q0, q1);
+              if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm,
+                             kErrEpilogueTimeout)) {
+                ok = false;
+              } else {
+                tc_fence_after();
+                tmem_ld8(tmem_base + t_col + acc * BN, nxt);
+              }
+            }
           }
-        } else {
+          const int q = (c < 8) ? qa0 : qa1;
+          if (MODE == kHybrid) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            W[i] += static_cast<int32_t>(P0[i]);
-            W[32 + i] += static_cast<int32_t>(P1[i]);
+            for (int i = 0; i < 8; ++i) W[8 * c + i] += q * static_cast<int32_t>(cur[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) W[8 * c + i] += static_cast<int32_t>(cur[i]);
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_acce + 8 * acc);
-        if (++acc == NACC) acc = 0, aphase ^= 1;
       }
       if (!ok) break;
-      // ---- convert, scale, round, store ----
-      float f;
+      // ---- convert, scale, round, store (direct 16-B stores of the row) ----
+      float f0, f1;
       if (MODE == kHybrid) {
         const float fa = row_ok ? __ldg(p.fa + static_cast<int64_t>(srow) * p.f_stride) : 0.f;
-        const float fbv =
-            col_ok ? __ldg(p.fb + (static_cast<int64_t>(ti.e) * p.nsb + jb) * p.f_stride) : 0.f;
-        f = fa * fbv;
+        const float* fbp = p.fb + (static_cast<int64_t>(ti.e) * p.nsb + jb) * p.f_stride;
+        f0 = c0_ok ? fa * __ldg(fbp) : 0.f;
+        f1 = c1_ok ? fa * __ldg(fbp + p.f_stride) : 0.f;
       } else if (p.a_row_scale != nullptr) {
         const int grow = __ldg(p.eo + ti.e) + (row_ok ? lrow : 0);
-        f = __ldg(p.a_row_scale + grow) * __ldg(p.b_expert_scale + ti.e);
+        f0 = f1 = __ldg(p.a_row_scale + grow) * __ldg(p.b_expert_scale + ti.e);
       } else {
-        f = p.alpha;
+        f0 = f1 = p.alpha;
       }
+      if (!(row_ok && c0_ok)) continue;
+      const int ncols = min(128, p.N - col0);
+      const int64_t row_off = static_cast<int64_t>(__ldg(p.eo + ti.e) + lrow) * p.N + col0;
       if constexpr (std::is_same<OutT, int32_t>::value) {
-        // raw accumulator output (verification mode): direct 16-B stores
-        if (row_ok && col_ok) {
-          const int ncols = min(64, p.N - col0);
-          int32_t* dst = static_cast<int32_t*>(p.out) +
-                         static_cast<int64_t>(__ldg(p.eo + ti.e) + lrow) * p.N + col0;
+        // raw accumulator output (verification mode)
+        int32_t* dst = static_cast<int32_t*>(p.out) + row_off;
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            if (4 * c < ncols)
-              *reinterpret_cast<int4*>(dst + 4 * c) =
-                  make_int4(W[4 * c], W[4 * c + 1], W[4 * c + 2], W[4 * c + 3]);
-        }
-        (void)f;
-        continue;
+        for (int c = 0; c < 32; ++c)
+          if (4 * c < ncols)
+            *reinterpret_cast<int4*>(dst + 4 * c) =
+                make_int4(W[4 * c], W[4 * c + 1], W[4 * c + 2], W[4 * c + 3]);
+        (void)f0;
+        (void)f1;
       } else {
-      if (pending_store) bulk_wait_read0();
-      uint32_t packed[32];
-      if (HAS_BIAS) {
-        const float* bp = p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0;
-        const int nvalid = p.N - col0;
+        OutT* dst = static_cast<OutT*>(p.out) + row_off;
+        const float* bp = HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0
+                                   : nullptr;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float b0 = (2 * i < nvalid) ? __ldg(bp + 2 * i) : 0.f;
-          const float b1 = (2 * i + 1 < nvalid) ? __ldg(bp + 2 * i + 1) : 0.f;
-          packed[i] = pack2<OutT>(fmaf(static_cast<float>(W[2 * i]), f, b0),
-                                  fmaf(static_cast<float>(W[2 * i + 1]), f, b1));
+        for (int c = 0; c < 16; ++c) {
+          if (8 * c >= ncols) continue;
+          const float f = (c < 8) ? f0 : f1;
+          uint32_t w4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int j = 8 * c + 2 * i;
+            if (HAS_BIAS) {
+              w4[i] = pack2<OutT>(fmaf(static_cast<float>(W[j]), f, __ldg(bp + j)),
+                                  fmaf(static_cast<float>(W[j + 1]), f, __ldg(bp + j + 1)));
+            } else {
+              w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[j]), f),
+                                  __fmul_rn(static_cast<float>(W[j + 1]), f));
+            }
+          }
+          *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          packed[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[2 * i]), f),
-                                  __fmul_rn(static_cast<float>(W[2 * i + 1]), f));
-      }
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        *reinterpret_cast<uint4*>(stage_row + 16 * c) =
-            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-      }
-      fence_proxy_async_smem();
-      if (row_ok && col_ok) {
-        const int ncols = min(64, p.N - col0);
-        OutT* dst = static_cast<OutT*>(p.out) +
-                    static_cast<int64_t>(__ldg(p.eo + ti.e) + lrow) * p.N + col0;
-        bulk_store(dst, stage_row_s, static_cast<uint32_t>(ncols * sizeof(OutT)));
-      }
-      bulk_commit();
-      pending_store = true;
       }
     }
-    bulk_wait0();
   }
 
   tc_fence_before();
@@ -568,6 +605,10 @@ int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const i
   p.k_pad = p.kt_total * BK - p.K;
   p.n_tiles = static_cast<int>((n + BN - 1) / BN);
   const int64_t upper_tiles = ((sum_m + BM - 1) / BM + E) * p.n_tiles;
+  {
+    const char* pf = getenv("I8MOE_GEMM_PREFETCH");
+    p.prefetch = pf ? atoi(pf) : 0;
+  }
   const int grid = static_cast<int>(std::min<int64_t>(num_sms(current_device()), upper_tiles));
   if (out_dtype == I8MOE_S32) {
     I8_REQUIRE(!has_bias, "the raw int32 accumulator output takes no bias");

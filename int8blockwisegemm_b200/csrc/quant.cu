@@ -1,5 +1,5 @@
 // Grouped per-(expert M-tile x 128-K block) INT8 activation quantisation
-// with the two-level (Q int32, F fp32) scale factorisation folded in.
+// with the two-level (Q int32, F fp32) scale factorisation.
 //
 // Semantics follow int8_hybrid_moe/quant.py of the reference:
 //   tile      = rows [eo[e] + i*tm, min(+tm, eo[e+1], M)) x cols [kb*128, +128)
@@ -12,25 +12,30 @@
 // gathered hidden row hidden[permuted_idx[r] / topk] (:284-357) and
 // silu(gate) * up of the w13 output (:440-511).
 //
-// Launch: one thread-block cluster of C = min(8, Kb) CTAs per scale row; CTA
-// rank j quantises K-blocks j, j+C, ...  Each CTA keeps its block scales in
-// shared memory; after a cluster barrier every CTA reads the scales of its
-// super-groups from its peers (distributed shared memory) and writes Q (and
-// the first CTA of a group writes F), so neither a global scale matrix nor a
-// second kernel is needed.
+// quant_kernel: a persistent grid (one CTA per SM) walks the (scale row,
+// K-block) tiles round-robin.  Warp 16 is the producer: it brings every tile
+// into a NS-deep shared-memory ring by TMA -- a dense 2-D box for contiguous
+// sources, four-row tile::gather4 boxes (row indices from permuted_idx) for
+// the permute gather -- and publishes the tile's row range next to it.  Warps
+// 0..15 form four independent consumer groups of four warps; group g takes
+// every fourth tile: pass 1 reduces the tile absmax from shared memory (warp
+// shuffles + a group named barrier), pass 2 quantises and stores the int8
+// rows, then the stage is released to the producer.  No CTA-wide barrier
+// sits on the hot path.  The block scale of every tile is written into the Q
+// buffer; scales_to_qf then factorises each (row, super-group) in place.
 //
-// x / scale is evaluated as x * (1/scale) first; whenever any product of a
-// thread lies within 1e-4 of a rounding tie (or is not finite) the thread
-// recomputes its elements with the IEEE quotient.  The product differs from
-// the IEEE quotient by less than 2e-5 for |x/scale| <= 128, so the rounded
-// integers are identical to round(x / scale) for every input.
-#include <cooperative_groups.h>
+// x / scale is evaluated as x * (1/scale) (packed f32x2 arithmetic); a
+// product farther than 3e-5 from a rounding tie rounds exactly as the IEEE
+// quotient does (the product is within 1.6e-5 of x/scale, the IEEE quotient
+// within 3.9e-6, for |x/scale| <= 128); the rare elements closer to a tie (or
+// not finite) are recomputed with the IEEE division.
+#include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace i8moe {
 
@@ -49,15 +54,12 @@ int read_quant_error(uint32_t* w, int clear) {
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kMaxCluster = 8;
-constexpr int kMaxKbPerCta = 64;  // Kb <= 512 (K <= 65536)
+constexpr int kGroupThreads = 128;
+constexpr int kMaxE = 2048;
 
 enum Mode { kDirect = 0, kGather = 1, kSilu = 2 };
 
 struct QuantArgs {
-  const void* src;
-  int64_t ld;      // elements per source row
   int M;           // rows of qA
   int K;           // quantised columns
   int topk;        // gather mode
@@ -66,13 +68,12 @@ struct QuantArgs {
   const int32_t* so;  // [E+1]
   int E;
   int Kb;
-  int csize;
-  float qmax;
-  int sg;
-  int nsg;
   int8_t* qA;
-  int32_t* Q;
-  float* F;
+  float* scale_out;  // [rows, Kb] block scales (the Q buffer, rewritten later)
+};
+
+struct TileInfo {
+  int s, kb, row_start, rows;
 };
 
 __device__ __forceinline__ float max_nan(float a, float b) {
@@ -81,13 +82,21 @@ __device__ __forceinline__ float max_nan(float a, float b) {
   return r;
 }
 
-// Low byte of the float bits of (y + 1.5*2^23) is round-to-nearest-even(y)
-// as a two's-complement byte for |y| < 2^22.
-__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d) {
-  const uint32_t lo = __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x0040);
-  const uint32_t hi = __byte_perm(__float_as_uint(c), __float_as_uint(d), 0x0040);
-  return __byte_perm(lo, hi, 0x5410);
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
 }
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
 
 __device__ __forceinline__ int8_t quant_exact(float x, float scale) {
   float v = __fdiv_rn(x, scale);
@@ -95,167 +104,363 @@ __device__ __forceinline__ int8_t quant_exact(float x, float scale) {
   return static_cast<int8_t>(static_cast<int>(roundf(v)));
 }
 
+// Bounded spin until the producer has issued item `it`.
+__device__ __forceinline__ bool wait_issued(const int* s_issued, int it, volatile int* abort) {
+  const volatile int* p = s_issued;
+  if (*p > it) return true;
+  const uint64_t t0 = globaltimer();
+  while (*p <= it) {
+    if (*abort) return false;
+    if (globaltimer() - t0 > I8MOE_WAIT_TIMEOUT_NS) {
+      *abort = 1;
+      atomicOr(&g_err_quant, kErrEpilogueTimeout);
+      return false;
+    }
+    __nanosleep(200);
+  }
+  __threadfence_block();
+  return true;
+}
+
+__device__ __forceinline__ int find_expert(const int* s_so, int E, int s) {
+  int lo = 0, hi = E;  // last e in [0, E) with so[e] <= s
+  while (lo + 1 < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (s_so[mid] <= s) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+
+// |x|-max of one 16-byte chunk (NaN-ignoring).
 template <typename T>
-__device__ __forceinline__ float elem(const uint4& v, int e) {
-  return Num<T>::to_f(reinterpret_cast<const T*>(&v)[e]);
+__device__ __forceinline__ float chunk_absmax(const uint4& v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+    __nv_bfloat162 m2 = __hmax2(__habs2(h[0]), __habs2(h[1]));
+    m2 = __hmax2(m2, __hmax2(__habs2(h[2]), __habs2(h[3])));
+    return fmaxf(__low2float(m2), __high2float(m2));
+  } else if constexpr (std::is_same<T, __half>::value) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    __half2 m2 = __hmax2(__habs2(h[0]), __habs2(h[1]));
+    m2 = __hmax2(m2, __hmax2(__habs2(h[2]), __habs2(h[3])));
+    return fmaxf(__low2float(m2), __high2float(m2));
+  } else {
+    const float* f = reinterpret_cast<const float*>(&v);
+    return fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+  }
+}
+
+// Exact SiLU of one chunk (the IEEE quotient for every element).
+template <typename T>
+__device__ __noinline__ uint4 silu_mul_chunk_exact(uint4 g, uint4 u) {
+  constexpr int EPC = 16 / sizeof(T);
+  uint4 o;
+#pragma unroll
+  for (int i = 0; i < EPC; ++i) {
+    const float gf = Num<T>::to_f(reinterpret_cast<const T*>(&g)[i]);
+    const float uf = Num<T>::to_f(reinterpret_cast<const T*>(&u)[i]);
+    const float sn = Num<T>::to_f(Num<T>::from_f(__fdiv_rn(gf, 1.0f + expf(-gf))));
+    reinterpret_cast<T*>(&o)[i] = Num<T>::from_f(sn * uf);
+  }
+  return o;
+}
+
+// act = dtype(dtype(g / (1 + exp(-g))) * up) for one chunk.  The quotient is
+// g * rcp(1 + exp(-g)), within 2.5 ulp of the IEEE quotient for |g| < 80;
+// the 16-bit rounding of the two agrees unless the value lies within 4 ulp
+// of a rounding midpoint of the storage type (or, for fp16, in its subnormal
+// range) -- such chunks are recomputed with the IEEE division.
+template <typename T>
+__device__ __forceinline__ uint4 silu_mul_chunk(const uint4& g, const uint4& u) {
+  if constexpr (sizeof(T) == 4) {
+    return silu_mul_chunk_exact<T>(g, u);
+  } else {
+    constexpr int EPC = 8;
+    uint4 o;
+    bool need = false;
+#pragma unroll
+    for (int i = 0; i < EPC; ++i) {
+      const float gf = Num<T>::to_f(reinterpret_cast<const T*>(&g)[i]);
+      const float uf = Num<T>::to_f(reinterpret_cast<const T*>(&u)[i]);
+      const float y = __fdividef(gf, 1.0f + expf(-gf));
+      const uint32_t b = __float_as_uint(y);
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        need |= (((b + 4u) & 0xFFFFu) - 0x8000u) <= 8u;
+      } else {
+        need |= (((b + 4u) & 0x1FFFu) - 0x1000u) <= 8u;
+        need |= !(fabsf(y) >= 6.103515625e-05f);
+      }
+      need |= !(fabsf(gf) < 80.0f);
+      const float sn = Num<T>::to_f(Num<T>::from_f(y));
+      reinterpret_cast<T*>(&o)[i] = Num<T>::from_f(sn * uf);
+    }
+    if (need) o = silu_mul_chunk_exact<T>(g, u);
+    return o;
+  }
+}
+
+// Fast INT8 quantisation of one chunk: x * inv (packed f32x2), rounded by the
+// 1.5*2^23 trick; returns false when an element lies within 3e-5 of a
+// rounding tie (or is not finite) so the caller takes the exact path.
+template <typename T>
+__device__ __forceinline__ bool quant_chunk_fast(const uint4& v, float inv,
+                                                 uint32_t (&words)[16 / sizeof(T) / 4]) {
+  constexpr int EPC = 16 / sizeof(T);
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t inv2 = f2_pack(inv, inv);
+  const uint64_t magic2 = f2_pack(kMagic, kMagic);
+  const uint64_t nmagic2 = f2_pack(-kMagic, -kMagic);
+  float dmax = 0.0f;
+#pragma unroll
+  for (int w = 0; w < EPC / 4; ++w) {
+    float f[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = Num<T>::to_f(reinterpret_cast<const T*>(&v)[4 * w + i]);
+    const uint64_t y01 = f2_mul(f2_pack(f[0], f[1]), inv2);
+    const uint64_t y23 = f2_mul(f2_pack(f[2], f[3]), inv2);
+    const uint64_t t01 = f2_add(y01, magic2);
+    const uint64_t t23 = f2_add(y23, magic2);
+    // d = y - rint(y): t - 1.5*2^23 is exact, negated by flipping the signs
+    const uint64_t d01 = f2_add(y01, f2_add(t01, nmagic2) ^ 0x8000000080000000ull);
+    const uint64_t d23 = f2_add(y23, f2_add(t23, nmagic2) ^ 0x8000000080000000ull);
+    dmax = max_nan(dmax, fabsf(f2_lo(d01)));
+    dmax = max_nan(dmax, fabsf(f2_hi(d01)));
+    dmax = max_nan(dmax, fabsf(f2_lo(d23)));
+    dmax = max_nan(dmax, fabsf(f2_hi(d23)));
+    const uint32_t lo = __byte_perm(static_cast<uint32_t>(t01), static_cast<uint32_t>(t01 >> 32), 0x0040);
+    const uint32_t hi = __byte_perm(static_cast<uint32_t>(t23), static_cast<uint32_t>(t23 >> 32), 0x0040);
+    words[w] = __byte_perm(lo, hi, 0x5410);
+  }
+  return dmax < 0.49997f;
+}
+
+// Exact reference rounding for one chunk: round_half_away(clamp(x / scale)).
+template <typename T>
+__device__ __noinline__ void quant_chunk_exact(uint4 v, float inv, float scale,
+                                               uint32_t (&words)[16 / sizeof(T) / 4]) {
+  constexpr int EPC = 16 / sizeof(T);
+  constexpr float kMagic = 12582912.0f;
+#pragma unroll
+  for (int i = 0; i < EPC; ++i) {
+    const float x = Num<T>::to_f(reinterpret_cast<const T*>(&v)[i]);
+    const float y = __fmul_rn(x, inv);
+    const float d = fabsf(y - (__fadd_rn(y, kMagic) - kMagic));
+    if (!(d < 0.49997f)) {
+      const uint32_t q = static_cast<uint8_t>(quant_exact(x, scale));
+      words[i / 4] = (words[i / 4] & ~(0xFFu << (8 * (i % 4)))) | (q << (8 * (i % 4)));
+    }
+  }
 }
 
 template <typename T, int TM, int MODE>
-__global__ void __launch_bounds__(kThreads) quant_kernel(QuantArgs a) {
-  constexpr int EPC = 16 / sizeof(T);    // elements per 16-B chunk
-  constexpr int CPR = 128 / EPC;         // chunks per 128-wide row segment
-  constexpr int RPP = kThreads / CPR;    // rows per pass
-  constexpr int PASSES = TM / RPP;
-  static_assert(TM % RPP == 0, "tile rows");
+struct QuantTile {
+  static constexpr int EPC = 16 / sizeof(T);      // elements per 16-B chunk
+  static constexpr int CPR = 128 / EPC;           // chunks per 128-wide row segment
+  static constexpr int ROWB = 128 * sizeof(T);    // bytes of one row segment
+  static constexpr int TILEB = TM * ROWB;
+  static constexpr int STAGEB = TILEB * (MODE == kSilu ? 2 : 1);
+  // ~96 KB of stages (two CTAs per SM) for the 16/32 KB tiles, the 64 KB
+  // SiLU tiles take 192 KB (one CTA per SM).
+  static constexpr int NS = STAGEB <= 16 * 1024 ? 6 : (STAGEB <= 64 * 1024 ? 3 : 1);
+  static constexpr int GROUPS = NS < 4 ? NS : 4;            // consumer groups of 4 warps
+  static constexpr int THREADS = GROUPS * kGroupThreads + 32;  // + producer warp
+  static constexpr int CHUNKS = TM * CPR;
+  static constexpr int CPT = CHUNKS / kGroupThreads;  // chunks per consumer thread
+  static_assert(CHUNKS % kGroupThreads == 0, "tile chunks");
+};
 
-  __shared__ float s_scale[kMaxKbPerCta];
-  __shared__ float s_red[kThreads / 32];
+template <typename T, int TM, int MODE>
+__global__ void __launch_bounds__(QuantTile<T, TM, MODE>::THREADS, 1)
+    quant_kernel(const __grid_constant__ CUtensorMap tmap, QuantArgs a) {
+  using TL = QuantTile<T, TM, MODE>;
+  constexpr int EPC = TL::EPC, CPR = TL::CPR, NS = TL::NS, CPT = TL::CPT;
+  constexpr int kGroups = TL::GROUPS, kThreads = TL::THREADS;
+  constexpr int kConsumerThreads = kGroups * kGroupThreads;
 
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = static_cast<int>(blockIdx.x % a.csize);
-  const int s = static_cast<int>(blockIdx.x / a.csize);
-  const int total = __ldg(a.so + a.E);
-  if (s >= total) return;  // the whole cluster shares s: uniform exit
+  extern __shared__ __align__(1024) uint8_t qsm_raw[];
+  uint8_t* stage_mem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(qsm_raw) + 1023) & ~uintptr_t(1023));
+  int* s_so = reinterpret_cast<int*>(stage_mem + NS * TL::STAGEB);
+  int* s_eo = s_so + (a.E + 1);
+  __shared__ __align__(8) uint64_t s_full[NS];
+  __shared__ __align__(8) uint64_t s_empty[NS];
+  __shared__ TileInfo s_info[NS];
+  __shared__ float s_red[4][2][4];
+  __shared__ int s_abort;
+  // Items handed to TMA so far.  Consumer groups take stages out of order, so
+  // a group may only wait on a stage's barrier once its own item has been
+  // issued there: then the barrier is pending exactly that item's phase and
+  // the parity wait cannot be satisfied by an older phase.
+  __shared__ int s_issued;
 
-  // expert owning scale row s: last e in [0, E) with so[e] <= s
-  int lo = 0, hi = a.E;
-  while (lo + 1 < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (__ldg(a.so + mid) <= s) lo = mid; else hi = mid;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i <= a.E; i += kThreads) {
+    s_so[i] = __ldg(a.so + i);
+    s_eo[i] = __ldg(a.eo + i);
   }
-  const int e = lo;
-  const int row_start = __ldg(a.eo + e) + (s - __ldg(a.so + e)) * TM;
-  const int row_end = min(min(__ldg(a.eo + e + 1), a.M), row_start + TM);
-
-  const int tid = threadIdx.x;
-  const int cr = tid % CPR;
-  const int r0 = tid / CPR;
-
-  // source row of every pass (gather: hidden row of the expanded row)
-  int srow[PASSES];
-#pragma unroll
-  for (int p = 0; p < PASSES; ++p) {
-    const int row = row_start + r0 + p * RPP;
-    srow[p] = row < row_end ? (MODE == kGather ? __ldg(a.pidx + row) / a.topk : row) : -1;
+  if (tid == 0) {
+    s_abort = 0;
+    s_issued = 0;
+    for (int st = 0; st < NS; ++st) {
+      mbar_init(smem_u32(&s_full[st]), 1);
+      mbar_init(smem_u32(&s_empty[st]), kGroupThreads / 32);
+    }
+    mbar_fence_init();
   }
-  const T* src = static_cast<const T*>(a.src);
+  __syncthreads();
+  const int total_items = s_so[a.E] * a.Kb;
+  const int n_items = blockIdx.x < total_items
+                          ? (total_items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
-  int nkb_local = 0;
-  for (int kb = rank; kb < a.Kb; kb += a.csize, ++nkb_local) {
-    const int col = kb * 128 + cr * EPC;
-    const bool colok = col < a.K;
-    uint4 v[PASSES];
+  if (warp == kConsumerThreads / 32) {
+    // ======================= producer warp =======================
+    if (lane == 0) tma_prefetch_desc(&tmap);
+    int last = -1;
+    bool ok = true;
+    // gather rows of the next item are loaded one item ahead
+    int src[4] = {0, 0, 0, 0};
+    auto item_rows = [&](int it, int& s, int& kb, int& row_start, int& row_end) {
+      const int g = blockIdx.x + it * gridDim.x;
+      s = g / a.Kb;
+      kb = g - s * a.Kb;
+      const int e = find_expert(s_so, a.E, s);
+      row_start = s_eo[e] + (s - s_so[e]) * TM;
+      row_end = min(min(s_eo[e + 1], a.M), row_start + TM);
+    };
+    auto load_src = [&](int it) {
+      int s, kb, rs, re;
+      item_rows(it, s, kb, rs, re);
 #pragma unroll
-    for (int p = 0; p < PASSES; ++p) {
-      v[p] = make_uint4(0, 0, 0, 0);
-      if (srow[p] >= 0 && colok) {
-        const T* rp = src + static_cast<int64_t>(srow[p]) * a.ld + col;
-        if (MODE == kSilu) {
-          const uint4 g = __ldg(reinterpret_cast<const uint4*>(rp));
-          const uint4 u = __ldg(reinterpret_cast<const uint4*>(rp + a.K));
-          T* o = reinterpret_cast<T*>(&v[p]);
-#pragma unroll
-          for (int i = 0; i < EPC; ++i) {
-            const float gf = elem<T>(g, i);
-            const float sl = __fdiv_rn(gf, 1.0f + expf(-gf));
-            const float sn = Num<T>::to_f(Num<T>::from_f(sl));
-            o[i] = Num<T>::from_f(sn * elem<T>(u, i));
-          }
-        } else {
-          v[p] = __ldg(reinterpret_cast<const uint4*>(rp));
-        }
+      for (int q = 0; q < 4; ++q) {
+        const int r = rs + 4 * lane + q;
+        src[q] = (4 * lane < TM && r < re) ? __ldg(a.pidx + r) / a.topk : 0;
+      }
+    };
+    if (MODE == kGather && n_items > 0) load_src(0);
+    for (int it = 0; it < n_items && ok; ++it) {
+      const int st = it % NS;
+      const uint32_t par = static_cast<uint32_t>(((it / NS) & 1) ^ 1);
+      if (!mbar_wait(smem_u32(&s_empty[st]), par, &s_abort, &g_err_quant, kErrProducerTimeout)) {
+        ok = false;
+        break;
+      }
+      int s, kb, row_start, row_end;
+      item_rows(it, s, kb, row_start, row_end);
+      const int col = kb * 128;
+      const uint32_t bar = smem_u32(&s_full[st]);
+      const uint32_t dst = smem_u32(stage_mem + st * TL::STAGEB);
+      if (lane == 0) s_info[st] = TileInfo{s, kb, row_start, row_end - row_start};
+      __syncwarp();
+      if (MODE == kGather) {
+        if (lane == 0) mbar_arrive_expect_tx(bar, TL::STAGEB);
+        __syncwarp();
+        if (4 * lane < TM)
+          tma_gather4(dst + lane * 4 * TL::ROWB, &tmap, bar, col, src[0], src[1], src[2], src[3]);
+        if (it + 1 < n_items) load_src(it + 1);
+      } else if (lane == 0) {
+        mbar_arrive_expect_tx(bar, TL::STAGEB);
+        tma_load_2d(dst, &tmap, bar, col, row_start);
+        if (MODE == kSilu) tma_load_2d(dst + TL::TILEB, &tmap, bar, col + a.K, row_start);
+      }
+      last = it;
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        *reinterpret_cast<volatile int*>(&s_issued) = it + 1;
       }
     }
-    // tile absmax (NaN-ignoring, as tl.max / fmaxf)
+    if (!ok && lane == 0) {
+      // never exit with TMA writes into this CTA's shared memory in flight
+      int no_abort = 0;
+      for (int it = max(0, last - NS + 1); it <= last; ++it)
+        mbar_wait(smem_u32(&s_full[it % NS]), static_cast<uint32_t>((it / NS) & 1), &no_abort,
+                  &g_err_quant, kErrDrainTimeout, 200000000ull);
+    }
+    return;
+  }
+
+  // ======================= consumer groups =======================
+  const int grp = warp >> 2;
+  const int gtid = tid & (kGroupThreads - 1);
+  const int gwarp = warp & 3;
+  int parity_red = 0;
+  for (int it = grp; it < n_items; it += kGroups) {
+    const int st = it % NS;
+    if (!wait_issued(&s_issued, it, &s_abort)) break;
+    if (!mbar_wait(smem_u32(&s_full[st]), static_cast<uint32_t>((it / NS) & 1), &s_abort,
+                   &g_err_quant, kErrEpilogueTimeout))
+      break;
+    const TileInfo ti = s_info[st];
+    uint8_t* tile = stage_mem + st * TL::STAGEB;
+    const int col0 = ti.kb * 128;
+
+    // ---- pass 1: (SiLU: act = dtype(silu(g)) * up, written back over g)
+    //      and the tile absmax (NaN-ignoring, as tl.max / fmaxf) ----
     float m = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < CPT; ++j) {
+      const int c = gtid + j * kGroupThreads;
+      const int r = c / CPR, cc = c % CPR;
+      if (r < ti.rows && col0 + cc * EPC < a.K) {
+        uint4* gp = reinterpret_cast<uint4*>(tile + r * TL::ROWB + cc * 16);
+        uint4 v = *gp;
+        if (MODE == kSilu) {
+          const uint4 u = *reinterpret_cast<const uint4*>(tile + TL::TILEB + r * TL::ROWB + cc * 16);
+          v = silu_mul_chunk<T>(v, u);
+          *gp = v;
+        }
+        m = fmaxf(m, chunk_absmax<T>(v));
+      }
+    }
+    const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+    if (lane == 0) s_red[grp][parity_red][gwarp] = __uint_as_float(mb);
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(kGroupThreads) : "memory");
+    float amax = s_red[grp][parity_red][0];
 #pragma unroll
-    for (int p = 0; p < PASSES; ++p)
-#pragma unroll
-      for (int i = 0; i < EPC; ++i) m = fmaxf(m, fabsf(elem<T>(v[p], i)));
-    unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
-    if ((tid & 31) == 0) s_red[tid >> 5] = __uint_as_float(mb);
-    __syncthreads();
-    float amax = s_red[0];
-#pragma unroll
-    for (int w = 1; w < kThreads / 32; ++w) amax = fmaxf(amax, s_red[w]);
-    __syncthreads();
+    for (int w = 1; w < 4; ++w) amax = fmaxf(amax, s_red[grp][parity_red][w]);
+    parity_red ^= 1;
     const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 127.0f);
     const float inv = __frcp_rn(scale);
-    if (tid == 0) s_scale[nkb_local] = scale;
+    if (gtid == 0) a.scale_out[static_cast<int64_t>(ti.s) * a.Kb + ti.kb] = scale;
 
-    // quantise: fast product path, packed as we go
-    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    constexpr int WPC = EPC / 4;           // packed words per chunk
-    uint32_t packed[PASSES][WPC];
-    float dmax = 0.0f;
-#pragma unroll
-    for (int p = 0; p < PASSES; ++p)
-#pragma unroll
-      for (int w = 0; w < WPC; ++w) {
-        float tt[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float y = __fmul_rn(elem<T>(v[p], 4 * w + i), inv);
-          tt[i] = __fadd_rn(y, kMagic);
-          dmax = max_nan(dmax, fabsf(y - (tt[i] - kMagic)));
-        }
-        packed[p][w] = pack4(tt[0], tt[1], tt[2], tt[3]);
+    // ---- pass 2: quantise and store ----
+#pragma unroll 1
+    for (int j = 0; j < CPT; ++j) {
+      const int c = gtid + j * kGroupThreads;
+      const int r = c / CPR, cc = c % CPR;
+      const int col = col0 + cc * EPC;
+      if (!(r < ti.rows && col < a.K)) continue;
+      const uint4 v = *reinterpret_cast<const uint4*>(tile + r * TL::ROWB + cc * 16);
+      uint32_t words[EPC / 4];
+      if (!quant_chunk_fast<T>(v, inv, words)) quant_chunk_exact<T>(v, inv, scale, words);
+      if (static_cast<unsigned>(ti.row_start + r) >= static_cast<unsigned>(a.M)) {
+        atomicOr(&g_err_quant, kErrBadIndex);  // never store outside qA
+        continue;
       }
-    if (!(dmax < 0.4999f)) {
-      // a product lies near a rounding tie (or is not finite): exact path
-#pragma unroll
-      for (int p = 0; p < PASSES; ++p)
-#pragma unroll
-        for (int w = 0; w < WPC; ++w) {
-          uint32_t word = 0;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int8_t q = quant_exact(elem<T>(v[p], 4 * w + i), scale);
-            word |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * i);
-          }
-          packed[p][w] = word;
-        }
-    }
-#pragma unroll
-    for (int p = 0; p < PASSES; ++p) {
-      if (!(srow[p] >= 0 && colok)) continue;
-      const int row = row_start + r0 + p * RPP;
-      int8_t* dst = a.qA + static_cast<int64_t>(row) * a.K + col;
-      if constexpr (WPC == 2) {
-        *reinterpret_cast<uint2*>(dst) = make_uint2(packed[p][0], packed[p][1]);
+      int8_t* dst = a.qA + static_cast<int64_t>(ti.row_start + r) * a.K + col;
+      if constexpr (EPC == 8) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[1]);
       } else {
-        *reinterpret_cast<uint32_t*>(dst) = packed[p][0];
+        *reinterpret_cast<uint32_t*>(dst) = words[0];
       }
     }
+    // release the stage to the producer
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&s_empty[st]));
   }
-
-  // two-level scale factorisation across the cluster
-  cluster.sync();
-  for (int li = tid; li < nkb_local; li += kThreads) {
-    const int kb = rank + li * a.csize;
-    const int g = kb / a.sg;
-    const int glo = g * a.sg;
-    const int ghi = min(glo + a.sg, a.Kb);
-    float smax = 0.0f;
-    for (int k2 = glo; k2 < ghi; ++k2) {
-      const float* peer = cluster.map_shared_rank(s_scale, k2 % a.csize);
-      smax = fmaxf(smax, fabsf(peer[k2 / a.csize]));
-    }
-    const float fg = __fdiv_rn(fmaxf(smax, 1e-12f), a.qmax);
-    const float qv = rintf(__fdiv_rn(s_scale[li], fg));
-    a.Q[static_cast<int64_t>(s) * a.Kb + kb] = __float2int_rz(qv);
-    if (kb == glo) a.F[static_cast<int64_t>(s) * a.nsg + g] = fg;
-  }
-  cluster.sync();
 }
 
-// Standalone Q/F factorisation of an fp32 scale matrix (one warp per row
-// and super-group).
-__global__ void quantize_scales_kernel(const float* __restrict__ scale, int rows, int kb,
-                                       float qmax, int sg, int nsg, int32_t* Q, float* F) {
+// Q/F factorisation of fp32 block scales, one warp per (row, super-group).
+// `scale` and `Q` may alias (in-place): every lane rewrites only the entries
+// it read, after the group maximum has been reduced.  When `rows_dev` is
+// non-null the row count is read from it (rows beyond it are skipped).
+__global__ void scales_to_qf(const float* scale, int rows, const int32_t* rows_dev, int kb,
+                             float qmax, int sg, int nsg, int32_t* Q, float* F) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= rows * nsg) return;
+  const int nrows = rows_dev ? min(rows, *rows_dev) : rows;
+  if (warp >= nrows * nsg) return;
   const int r = warp / nsg, g = warp % nsg;
   const int lo = g * sg, hi = min(lo + sg, kb);
   float m = 0.0f;
@@ -313,54 +518,90 @@ __global__ void __launch_bounds__(1024) scale_offsets_kernel(const int32_t* eo, 
 
 int dtype_size(int dtype) { return dtype == I8MOE_FP32 ? 4 : 2; }
 
-template <typename T, int TM, int MODE>
-int launch_quant_t(const QuantArgs& a, int rows_upper, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(rows_upper * a.csize), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.csize;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  I8_CUDA(cudaLaunchKernelEx(&cfg, quant_kernel<T, TM, MODE>, a));
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_q = nullptr;
+std::once_flag g_encode_q_once;
+
+int encode_fn() {
+  std::call_once(g_encode_q_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode_q = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode_q) return set_error(I8MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   return I8MOE_OK;
 }
 
-template <int MODE>
-int launch_quant_mode(int dtype, int tm, const QuantArgs& a, int rows_upper, cudaStream_t st) {
-  if (dtype == I8MOE_BF16) {
-    return tm == 64 ? launch_quant_t<__nv_bfloat16, 64, MODE>(a, rows_upper, st)
-                    : launch_quant_t<__nv_bfloat16, 128, MODE>(a, rows_upper, st);
-  } else if (dtype == I8MOE_FP16) {
-    return tm == 64 ? launch_quant_t<__half, 64, MODE>(a, rows_upper, st)
-                    : launch_quant_t<__half, 128, MODE>(a, rows_upper, st);
-  }
-  return tm == 64 ? launch_quant_t<float, 64, MODE>(a, rows_upper, st)
-                  : launch_quant_t<float, 128, MODE>(a, rows_upper, st);
+// 2-D tensor map over a row-major [rows, cols] matrix with a box of
+// 128 columns x box_rows rows, no swizzle, zero fill out of bounds.
+int make_src_map(CUtensorMap* m, const void* base, int dtype, int64_t rows, int64_t cols,
+                 int box_rows) {
+  const CUtensorMapDataType dt = dtype == I8MOE_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : dtype == I8MOE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * dtype_size(dtype))};
+  cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode_q(m, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(I8MOE_ERR_CUDA, "cuTensorMapEncodeTiled(quant source) failed");
+  return I8MOE_OK;
 }
 
-int launch_quant(int mode, const void* src, int dtype, int64_t ld, int64_t M, int64_t K,
-                 const int32_t* pidx, int64_t topk, const int32_t* eo, int64_t E, int64_t tm,
-                 int64_t block_k, int64_t q_max, int64_t sg, int8_t* qA, int32_t* Q, float* F,
-                 int32_t* so, int so_ready, cudaStream_t st) {
+template <typename T, int TM, int MODE>
+int launch_quant_t(const CUtensorMap& tmap, QuantArgs a, int rows_upper, cudaStream_t st) {
+  using TL = QuantTile<T, TM, MODE>;
+  auto kern = quant_kernel<T, TM, MODE>;
+  const int smem = TL::NS * TL::STAGEB + 2 * (a.E + 1) * 4 + 1024;
+  I8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, TL::THREADS, smem) !=
+          cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  const int64_t items_upper = static_cast<int64_t>(rows_upper) * a.Kb;
+  const int grid = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(static_cast<int64_t>(per_sm) * num_sms(current_device()), items_upper)));
+  kern<<<grid, TL::THREADS, smem, st>>>(tmap, a);
+  return check_launch("quant");
+}
+
+template <int MODE>
+int launch_quant_mode(int dtype, int tm, const CUtensorMap& tmap, const QuantArgs& a,
+                      int rows_upper, cudaStream_t st) {
+  // (one CTA per SM; see quant_kernel)
+  if (dtype == I8MOE_BF16) {
+    return tm == 64 ? launch_quant_t<__nv_bfloat16, 64, MODE>(tmap, a, rows_upper, st)
+                    : launch_quant_t<__nv_bfloat16, 128, MODE>(tmap, a, rows_upper, st);
+  } else if (dtype == I8MOE_FP16) {
+    return tm == 64 ? launch_quant_t<__half, 64, MODE>(tmap, a, rows_upper, st)
+                    : launch_quant_t<__half, 128, MODE>(tmap, a, rows_upper, st);
+  }
+  return tm == 64 ? launch_quant_t<float, 64, MODE>(tmap, a, rows_upper, st)
+                  : launch_quant_t<float, 128, MODE>(tmap, a, rows_upper, st);
+}
+
+// src rows/cols describe the TMA source: direct [M, K], gather [n_src, K],
+// silu [M, 2K].
+int launch_quant(int mode, const void* src, int dtype, int64_t src_rows, int64_t src_cols,
+                 int64_t M, int64_t K, const int32_t* pidx, int64_t topk, const int32_t* eo,
+                 int64_t E, int64_t tm, int64_t block_k, int64_t q_max, int64_t sg, int8_t* qA,
+                 int32_t* Q, float* F, int32_t* so, int so_ready, cudaStream_t st) {
   I8_REQUIRE(dtype == I8MOE_BF16 || dtype == I8MOE_FP16 || dtype == I8MOE_FP32,
              "quant: A must be float32, float16 or bfloat16");
   I8_REQUIRE(block_k == 128, "quant: block_k must be 128 (the only quant block the GEMM reads)");
   I8_REQUIRE(tm == 64 || tm == 128, "quant: tile_m must be 64 or 128");
   I8_REQUIRE(sg > 0 && q_max > 0, "quant: super_group_size and q_max must be positive");
-  I8_REQUIRE(E >= 1 && E <= 65536, "quant: expert_offsets must have 2..65537 entries");
+  I8_REQUIRE(E >= 1 && E <= kMaxE, "quant: number of experts must be in [1, %d]", kMaxE);
   I8_REQUIRE(K % 8 == 0, "quant: K must be a multiple of 8");
   I8_REQUIRE(M >= 0 && M < (int64_t(1) << 31), "quant: bad M");
   const int64_t Kb = (K + block_k - 1) / block_k;
-  const int csize = static_cast<int>(std::min<int64_t>(kMaxCluster, std::max<int64_t>(Kb, 1)));
-  I8_REQUIRE((Kb + csize - 1) / csize <= kMaxKbPerCta, "quant: K too large (max 65536)");
-  const uintptr_t al = reinterpret_cast<uintptr_t>(src) | static_cast<uintptr_t>(ld * dtype_size(dtype));
-  I8_REQUIRE(al % 16 == 0, "quant: source rows must be 16-byte aligned");
+  I8_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0, "quant: source must be 16-byte aligned");
   I8_REQUIRE(reinterpret_cast<uintptr_t>(qA) % 8 == 0, "quant: qA must be 8-byte aligned");
   if (!so_ready) {
     scale_offsets_kernel<<<1, 1024, 0, st>>>(eo, static_cast<int>(E), static_cast<int>(tm), so);
@@ -368,10 +609,13 @@ int launch_quant(int mode, const void* src, int dtype, int64_t ld, int64_t M, in
     if (rc) return rc;
   }
   const int64_t rows_upper = (M + tm - 1) / tm + E;
-  if (M == 0 || K == 0) return I8MOE_OK;
+  if (M == 0 || K == 0 || src_rows == 0) return I8MOE_OK;
+  int rc = encode_fn();
+  if (rc) return rc;
+  CUtensorMap tmap;
+  rc = make_src_map(&tmap, src, dtype, src_rows, src_cols, mode == kGather ? 1 : static_cast<int>(tm));
+  if (rc) return rc;
   QuantArgs a{};
-  a.src = src;
-  a.ld = ld;
   a.M = static_cast<int>(M);
   a.K = static_cast<int>(K);
   a.topk = static_cast<int>(topk);
@@ -380,20 +624,19 @@ int launch_quant(int mode, const void* src, int dtype, int64_t ld, int64_t M, in
   a.so = so;
   a.E = static_cast<int>(E);
   a.Kb = static_cast<int>(Kb);
-  a.csize = csize;
-  a.qmax = static_cast<float>(q_max);
-  a.sg = static_cast<int>(sg);
-  a.nsg = static_cast<int>((Kb + sg - 1) / sg);
   a.qA = qA;
-  a.Q = Q;
-  a.F = F;
-  const int ru = static_cast<int>(rows_upper);
+  a.scale_out = reinterpret_cast<float*>(Q);  // rewritten in place by scales_to_qf
+  const int ru = static_cast<int>(std::min<int64_t>(rows_upper, INT32_MAX / std::max<int64_t>(Kb, 1)));
   const int t = static_cast<int>(tm);
-  int rc;
-  if (mode == kDirect) rc = launch_quant_mode<kDirect>(dtype, t, a, ru, st);
-  else if (mode == kGather) rc = launch_quant_mode<kGather>(dtype, t, a, ru, st);
-  else rc = launch_quant_mode<kSilu>(dtype, t, a, ru, st);
+  if (mode == kDirect) rc = launch_quant_mode<kDirect>(dtype, t, tmap, a, ru, st);
+  else if (mode == kGather) rc = launch_quant_mode<kGather>(dtype, t, tmap, a, ru, st);
+  else rc = launch_quant_mode<kSilu>(dtype, t, tmap, a, ru, st);
   if (rc) return rc;
+  const int nsg = static_cast<int>((Kb + sg - 1) / sg);
+  const int64_t warps = static_cast<int64_t>(ru) * nsg;
+  scales_to_qf<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const float*>(Q), ru, so + E, static_cast<int>(Kb), static_cast<float>(q_max),
+      static_cast<int>(sg), nsg, Q, F);
   return check_launch("quant");
 }
 
@@ -417,7 +660,7 @@ int i8moe_quant_grouped(const void* A, int dtype, int64_t M, int64_t K,
                         int64_t block_k, int64_t q_max, int64_t super_group_size, int8_t* qA,
                         int32_t* Q, float* F, int32_t* scale_offsets, int scale_offsets_ready,
                         i8moe_stream_t stream) {
-  return launch_quant(kDirect, A, dtype, K, M, K, nullptr, 1, expert_offsets, n_expert, tile_m,
+  return launch_quant(kDirect, A, dtype, M, K, M, K, nullptr, 1, expert_offsets, n_expert, tile_m,
                       block_k, q_max, super_group_size, qA, Q, F, scale_offsets,
                       scale_offsets_ready, static_cast<cudaStream_t>(stream));
 }
@@ -428,9 +671,8 @@ int i8moe_quant_permute(const void* hidden, int dtype, int64_t n_token, int64_t 
                         int64_t block_k, int64_t q_max, int64_t super_group_size, int8_t* qA,
                         int32_t* Q, float* F, int32_t* scale_offsets, int scale_offsets_ready,
                         i8moe_stream_t stream) {
-  (void)n_token;
   I8_REQUIRE(topk > 0, "quant_permute: topk must be positive");
-  return launch_quant(kGather, hidden, dtype, K, M, K, permuted_idx, topk, expert_offsets,
+  return launch_quant(kGather, hidden, dtype, n_token, K, M, K, permuted_idx, topk, expert_offsets,
                       n_expert, tile_m, block_k, q_max, super_group_size, qA, Q, F,
                       scale_offsets, scale_offsets_ready, static_cast<cudaStream_t>(stream));
 }
@@ -440,7 +682,7 @@ int i8moe_quant_silu(const void* mm1, int dtype, int64_t M, int64_t N,
                      int64_t block_k, int64_t q_max, int64_t super_group_size, int8_t* qA,
                      int32_t* Q, float* F, int32_t* scale_offsets, int scale_offsets_ready,
                      i8moe_stream_t stream) {
-  return launch_quant(kSilu, mm1, dtype, 2 * N, M, N, nullptr, 1, expert_offsets, n_expert,
+  return launch_quant(kSilu, mm1, dtype, M, 2 * N, M, N, nullptr, 1, expert_offsets, n_expert,
                       tile_m, block_k, q_max, super_group_size, qA, Q, F, scale_offsets,
                       scale_offsets_ready, static_cast<cudaStream_t>(stream));
 }
@@ -454,8 +696,8 @@ int i8moe_quantize_scales(const float* scale, int64_t rows, int64_t kb, int64_t 
   const int64_t nsg = (kb + super_group_size - 1) / super_group_size;
   const int64_t warps = rows * nsg;
   const int grid = static_cast<int>((warps * 32 + 255) / 256);
-  quantize_scales_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      scale, static_cast<int>(rows), static_cast<int>(kb), static_cast<float>(q_max),
+  scales_to_qf<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      scale, static_cast<int>(rows), nullptr, static_cast<int>(kb), static_cast<float>(q_max),
       static_cast<int>(super_group_size), static_cast<int>(nsg), Q, F);
   return check_launch("quantize_scales");
 }

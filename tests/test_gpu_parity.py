@@ -6,9 +6,9 @@ Tolerances:
     offsets, the raw int32 GEMM accumulators, GEMM bf16/fp16 outputs,
     per-tensor GEMM outputs;
   * SiLU-dependent values (silu_and_mul, the a2 int8 activations): the
-    device expf and the host exp may differ by one float32 ulp, which can flip
-    one bf16 rounding; such flips must be rare (counted and bounded) and at
-    most one step;
+    device expf and the host exp may differ by a float32 ulp or two, which can
+    flip one bf16/fp16 rounding; such flips must be rare (counted and bounded)
+    and at most one step (fp32 storage: a few float32 ulp);
   * unpermute: the oracle emulates fp32 FMA in float64 (double rounding can
     differ by one float32 ulp), so one bf16/fp16 ulp on a tiny fraction;
   * final MoE output: max|y - ref| / max|ref| <= 1e-2.
@@ -309,7 +309,11 @@ def test_silu_and_mul(m, dtype):
     m.ops.silu_and_mul(out, x)
     exp = ref.silu_and_mul(npf(x), dtype)
     ud = ulp_diff(npf(out), exp, dtype)
-    assert ud.max() <= 1 and (ud > 0).mean() < 1e-3
+    if dtype == "fp32":
+        # no 16-bit rounding hides the device expf (<= 2 ulp) here
+        assert ud.max() <= 8
+    else:
+        assert ud.max() <= 1 and (ud > 0).mean() < 1e-3
 
 
 @pytest.mark.parametrize("dtype,ep", [("bf16", False), ("fp16", False), ("fp32", False),
