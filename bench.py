@@ -272,14 +272,23 @@ def time_w13_gemm(pkg, cfg, st, tr, iters=20):
             tr["a1_so"])
     for _ in range(3):
         fn(*args)
+    torch.cuda.synchronize()
+    # The launches are replayed from a CUDA graph so that host-side launch
+    # cost (op dispatch, tensor-map encoding) does not leave the GPU idle
+    # between them; the events then bracket device time only.
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn(*args)
+    g.replay()
+    torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
     e0.record(s)
-    for _ in range(iters):
-        fn(*args)
+    g.replay()
     e1.record(s)
     torch.cuda.synchronize()
+    del g
     return e0.elapsed_time(e1) / iters * 1e-3
 
 

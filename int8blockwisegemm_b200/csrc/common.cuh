@@ -188,6 +188,15 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const void* desc, uint
       : "memory");
 }
 
+// Tiled shared -> global tensor store (bulk group); the coordinates must be
+// non-negative and x * element size a multiple of 16 bytes.
+__device__ __forceinline__ void tma_store_2d(const void* desc, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+
 // Bulk (non-tensor) shared -> global copy; both addresses 16-B aligned,
 // size a multiple of 16.
 __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
@@ -206,6 +215,15 @@ __device__ __forceinline__ void bulk_wait0() {
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 4-byte global -> shared asynchronous copy (no register destination), and
+// the wait for all of this thread's outstanding ones.
+__device__ __forceinline__ void cp_async4(uint32_t sdst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sdst), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------

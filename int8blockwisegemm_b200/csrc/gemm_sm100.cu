@@ -11,7 +11,7 @@
 //     out = dtype(float(sum_k a*b) * alpha) with alpha per tensor, or
 //     per-token x per-expert (extension).
 //
-// Structure (one CTA per SM, 10 warps; tiles of 128 rows x 256 columns):
+// Structure (one CTA per SM, 18 warps; tiles of 128 rows x 256 columns):
 //   warp 0      TMA producer: A tile [128 rows x 128 K] and B tile
 //               [BN x 128 K] per K-tile, 128-byte swizzle, into a STAGES-deep
 //               shared-memory ring guarded by full/empty mbarriers.
@@ -21,14 +21,17 @@
 //               accumulator buffers (256 columns each); tcgen05.commit frees
 //               the smem stage and, at the end of a quant block, signals the
 //               epilogue.
-//   warps 2..9  epilogue: TMEM lane quadrant = warp % 4, column half =
-//               (warp - 2) / 4.  Each thread owns one output row and 128
-//               columns: tcgen05.ld the block partial in 8-column chunks
-//               (the next chunk's load overlaps this chunk's accumulation),
+//   warps 2..17 epilogue: TMEM lane quadrant = warp % 4, column quarter =
+//               (warp - 2) / 4.  Each thread owns one output row and 64
+//               columns: tcgen05.ld the block partial in 16-column chunks
+//               (other warps' accumulation covers each load's latency),
 //               release the TMEM buffer, W += q * P (int32 IMAD); after the
 //               last block convert, scale, round and store the row with 16-B
 //               stores (rows beyond the expert are not stored, so
 //               neighbouring experts are never overwritten).
+//               The hybrid format costs one integer multiply-add per output
+//               element per quant block, which at 128-deep blocks matches the
+//               tensor-core rate; 16 warps keep that pipe fed.
 // Tiles: (expert, 128-row m-tile, BN-col n-tile), m-tile major, walked
 // round-robin by the persistent CTAs; the per-expert m-tile prefix is built
 // in shared memory from problem_sizes at kernel start (no host loop, no
@@ -66,9 +69,9 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 128;  // bytes == int8 elements per K-tile
-constexpr int STAGES = 4;
+constexpr int STAGES = 3;
 constexpr int NACC = 2;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue warps
 constexpr int kMaxExperts = 1024;
 constexpr int kTileABytes = BM * BK;
@@ -103,11 +106,19 @@ struct GemmParams {
 struct SmemLayout {
   static constexpr int kA = 0;
   static constexpr int kB = kA + STAGES * kTileABytes;
-  static constexpr int kBar = kB + STAGES * kTileBBytes;  // 8-B aligned
+  // per-epilogue-warp output staging (32 rows x 64 B, 64-byte swizzle)
+  static constexpr int kStg = kB + STAGES * kTileBBytes;  // 1024-B aligned
+  static constexpr int kStgWarpBytes = 32 * 64;
+  static constexpr int kBar = kStg + kEpiWarps * kStgWarpBytes;  // 8-B aligned
   static constexpr int kNumBars = 2 * STAGES + 2 * NACC + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;   // tmem base, abort flag
-  static constexpr int kPrefix = kMisc + 16;          // mt_prefix[E+1], so_prefix[E+1]
-  static constexpr int bytes(int E) { return kPrefix + 2 * (E + 1) * 4 + 32; }
+  // per-epilogue-thread slots (Q_A, Q_B per tile parity; F_A, F_B of the
+  // current tile), then the per-expert tables: m-tile prefix, scale-row
+  // offset, row count, first row
+  static constexpr int kSlots = kMisc + 16;
+  static constexpr int kSlotArray = 4 * 32 * kEpiWarps;
+  static constexpr int kPrefix = kSlots + 6 * kSlotArray;
+  static constexpr int bytes(int E) { return kPrefix + 4 * (E + 1) * 4 + 32; }
 };
 
 template <typename OutT>
@@ -183,7 +194,8 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const int* mt_prefix, int
 template <int MODE, bool HAS_BIAS, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -201,12 +213,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* s_tmp = reinterpret_cast<int*>(smem + SmemLayout::kA);  // scratch before the first TMA
   int* mt_prefix = reinterpret_cast<int*>(smem + SmemLayout::kPrefix);
   int* so_prefix = mt_prefix + (p.E + 1);
+  int* m_rows = so_prefix + (p.E + 1);
+  int* e_row0 = m_rows + (p.E + 1);
 
-  // ---- prologue: tile prefix over experts ----
+  // ---- prologue: per-expert tables (tile prefix, scale rows, rows) ----
+  // Kept in shared memory so a tile's coordinates resolve without global
+  // loads on the epilogue's critical path.
   for (int e = threadIdx.x; e < p.E; e += kThreads) {
     const int m = max(0, __ldg(p.ps + 3 * e));
     mt_prefix[e] = (m + BM - 1) / BM;
-    so_prefix[e] = (m + p.tile_m - 1) / p.tile_m;
+    so_prefix[e] = p.so ? __ldg(p.so + e) : (m + p.tile_m - 1) / p.tile_m;
+    m_rows[e] = m;
+    e_row0[e] = __ldg(p.eo + e);
   }
   if (threadIdx.x == 0) *s_abort = 0;
   __syncthreads();
@@ -252,10 +270,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // prefetched into L2 so first touches of weight tiles in HBM overlap.
       int t = blockIdx.x;
       TileInfo ti = decode_tile(t < total_tiles ? t : 0, mt_prefix, p.E, p.n_tiles);
-      int row0 = __ldg(p.eo + ti.e) + ti.mt * BM;
+      int row0 = e_row0[ti.e] + ti.mt * BM;
       int tn = t + gridDim.x;
       TileInfo tin = decode_tile(tn < total_tiles ? tn : 0, mt_prefix, p.E, p.n_tiles);
-      int row0n = __ldg(p.eo + tin.e) + tin.mt * BM;
+      int row0n = e_row0[tin.e] + tin.mt * BM;
       for (; t < total_tiles && ok; t += gridDim.x) {
         const int n0 = ti.nt * BN;
         for (int kt = 0; kt < p.kt_total; ++kt) {
@@ -294,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tn += gridDim.x;
         if (tn < total_tiles) {
           tin = decode_tile(tn, mt_prefix, p.E, p.n_tiles);
-          row0n = __ldg(p.eo + tin.e) + tin.mt * BM;
+          row0n = e_row0[tin.e] + tin.mt * BM;
         }
       }
       if (!ok) {
@@ -315,38 +333,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t aphase = 0;
       bool ok = true;
       bool any = false;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        for (int qb = 0; qb < p.nq && ok; ++qb) {
-          if (!mbar_wait(bar_acce + 8 * acc, aphase ^ 1, s_abort, &g_err_gemm, kErrMmaTimeout)) {
+      // The issuer needs no tile coordinates: it walks this CTA's quant
+      // blocks in order (tiles blockIdx.x, +gridDim.x, ...), one TMEM
+      // accumulator buffer per block.  Shared memory filled by TMA is made
+      // visible by the full-barrier wait itself; the tcgen05 fence is only
+      // needed after the accumulator hand-back, which the epilogue's
+      // tcgen05.ld precede.
+      const int my_tiles =
+          blockIdx.x < total_tiles ? (total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const int n_blocks = my_tiles * p.nq;
+      int qb = 0;
+      for (int i = 0; i < n_blocks; ++i) {
+        if (!mbar_wait(bar_acce + 8 * acc, aphase ^ 1, s_abort, &g_err_gemm, kErrMmaTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        const int kt0 = qb * p.ktpq;
+        const int kt1 = min(kt0 + p.ktpq, p.kt_total);
+        for (int kt = kt0; kt < kt1; ++kt) {
+          if (!mbar_wait(bar_full + 8 * stage, phase, s_abort, &g_err_gemm, kErrMmaTimeout)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t d_tmem = tmem_base + acc * BN;
-          const int kt0 = qb * p.ktpq;
-          const int kt1 = min(kt0 + p.ktpq, p.kt_total);
-          for (int kt = kt0; kt < kt1; ++kt) {
-            if (!mbar_wait(bar_full + 8 * stage, phase, s_abort, &g_err_gemm, kErrMmaTimeout)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t a_addr = sbase + SmemLayout::kA + stage * kTileABytes;
-            const uint32_t b_addr = sbase + SmemLayout::kB + stage * kTileBBytes;
+          const uint32_t a_addr = sbase + SmemLayout::kA + stage * kTileABytes;
+          const uint32_t b_addr = sbase + SmemLayout::kB + stage * kTileBBytes;
 #pragma unroll
-            for (int k = 0; k < BK / 32; ++k) {
-              const uint64_t ad = sw128_kmajor_desc(a_addr + k * 32);
-              const uint64_t bd = sw128_kmajor_desc(b_addr + k * 32);
-              umma_i8(d_tmem, ad, bd, kIdesc, (kt > kt0 || k > 0) ? 1u : 0u);
-            }
-            any = true;
-            umma_commit(bar_empty + 8 * stage);
-            if (++stage == STAGES) stage = 0, phase ^= 1;
+          for (int k = 0; k < BK / 32; ++k) {
+            const uint64_t ad = sw128_kmajor_desc(a_addr + k * 32);
+            const uint64_t bd = sw128_kmajor_desc(b_addr + k * 32);
+            umma_i8(d_tmem, ad, bd, kIdesc, (kt > kt0 || k > 0) ? 1u : 0u);
           }
-          if (!ok) break;
-          umma_commit(bar_accf + 8 * acc);
-          if (++acc == NACC) acc = 0, aphase ^= 1;
+          any = true;
+          umma_commit(bar_empty + 8 * stage);
+          if (++stage == STAGES) stage = 0, phase ^= 1;
         }
+        if (!ok) break;
+        umma_commit(bar_accf + 8 * acc);
+        if (++acc == NACC) acc = 0, aphase ^= 1;
+        if (++qb == p.nq) qb = 0;
       }
       // wait for every issued MMA before TMEM can be released
       if (any) {
@@ -357,121 +383,211 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ================= epilogue (8 warps) =================
-    // TMEM lane quadrant = warp % 4 (hardware rule), column half =
-    // (warp - 2) / 4: each thread owns one row and 128 columns (two 64-column
-    // weight-scale blocks) of the 128 x 256 tile.
+    // ================= epilogue (16 warps) =================
+    // TMEM lane quadrant = warp % 4 (hardware rule), column quarter =
+    // (warp - 2) / 4: each thread owns one row and 64 columns (one 64-column
+    // weight-scale block) of the 128 x 256 tile, so a single Q_A * Q_B factor
+    // applies to all of its columns in a quant block.  Four warps share each
+    // SM sub-partition, which is what keeps the integer multiply-add pipe
+    // busy while the other warps wait for their TMEM loads.
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int cq = (warp - 2) >> 2;
     const int rl = quad * 32 + lane;  // row within the tile == TMEM lane
-    const uint32_t t_col = (static_cast<uint32_t>(quad * 32) << 16) + half * 128;
+    const uint32_t t_col = (static_cast<uint32_t>(quad * 32) << 16) + cq * 64;
     int acc = 0;
     uint32_t aphase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
-      const int m_e = __ldg(p.ps + 3 * ti.e);
-      const int lrow = ti.mt * BM + rl;
-      const bool row_ok = lrow < m_e;
-      const int col0 = ti.nt * BN + half * 128;
-      const bool c0_ok = col0 < p.N;
-      const bool c1_ok = col0 + 64 < p.N;
-      const int so_e = p.so ? __ldg(p.so + ti.e) : so_prefix[ti.e];
-      const int srow = so_e + (row_ok ? lrow : 0) / p.tile_m;
-      const int jb = col0 / 64;
-      const int32_t* qa_row = p.qa + static_cast<int64_t>(srow) * p.q_stride;
-      const int32_t* qb_col = p.qb + (static_cast<int64_t>(ti.e) * p.nsb + jb) * p.q_stride;
-      int q0 = 1, q1 = 1;  // Q_A * Q_B of the two 64-column blocks, current q-block
-      auto qfac = [&](int qb, int& r0, int& r1) {
-        if (MODE != kHybrid) { r0 = r1 = 1; return; }
-        const int qa = row_ok ? __ldg(qa_row + qb) : 0;
-        r0 = c0_ok ? qa * __ldg(qb_col + qb) : 0;
-        r1 = c1_ok ? qa * __ldg(qb_col + p.q_stride + qb) : 0;
-      };
-      int32_t W[128];
-#pragma unroll
-      for (int i = 0; i < 128; ++i) W[i] = 0;
-      // Pipelined at 8-column granularity: chunk c+1 (or the next block's
-      // chunk 0) is in flight while chunk c is accumulated; the accumulator
-      // buffer goes back to the MMA warp as soon as its last chunk landed.
-      uint32_t P0[8], P1[8];
-      qfac(0, q0, q1);
-      if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm, kErrEpilogueTimeout)) {
-        ok = false;
-        break;
+    // Every lane of a warp shares one scale row (a 32-row group never
+    // straddles a tile_m boundary) and one 64-column weight block, so the
+    // factor Q_A * Q_B of a quant block is warp-uniform: lane l holds that
+    // of block (qb0 + l), and each block's factor is broadcast by shuffle.
+    // The next tile's Q factors and this tile's F factors travel by cp.async
+    // into per-thread shared-memory slots while the accumulation runs, so
+    // they take no registers from the accumulator.
+    // Slots: [Q_A, Q_B] for even local tiles, [Q_A, Q_B] for odd ones, then
+    // F_A, F_B; a slot pair is refilled only for the tile after next, so an
+    // asynchronous write never meets a pending read of the same slot.
+    const uint32_t s_slot = sbase + SmemLayout::kSlots + 4 * (threadIdx.x - 64);
+    constexpr uint32_t kSA = SmemLayout::kSlotArray;
+    const uint32_t s_fa = s_slot + 4 * kSA;
+    const uint32_t s_fb = s_slot + 5 * kSA;
+    auto ld_s32 = [](uint32_t a) {
+      int v;
+      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+      return v;
+    };
+    auto st_s32 = [](uint32_t a, int v) {
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+    };
+    // Q_A / Q_B of quant block (qb0 + lane) of tile t, synchronously
+    auto tile_q = [&](int t, int qb0) -> int {
+      const TileInfo u = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+      const int wrow = u.mt * BM + quad * 32;
+      const int col = u.nt * BN + cq * 64;
+      const int qb = qb0 + lane;
+      if (MODE != kHybrid || wrow >= m_rows[u.e] || col >= p.N || qb >= p.nq) return 0;
+      const int srow = so_prefix[u.e] + wrow / p.tile_m;
+      return __ldg(p.qa + static_cast<int64_t>(srow) * p.q_stride + qb) *
+             __ldg(p.qb + (static_cast<int64_t>(u.e) * p.nsb + col / 64) * p.q_stride + qb);
+    };
+    // Q_A / Q_B of quant blocks 0..31 (one per lane) of tile t, into the
+    // slot pair `par` asynchronously
+    auto fetch_q = [&](int t, int par) {
+      const uint32_t s_qa = s_slot + (2 * par) * kSA, s_qb = s_qa + kSA;
+      const int qb0 = 0;
+      bool any = false;
+      if (MODE == kHybrid && t < total_tiles) {
+        const TileInfo u = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+        const int wrow = u.mt * BM + quad * 32;
+        const int col = u.nt * BN + cq * 64;
+        const int qb = qb0 + lane;
+        if (wrow < m_rows[u.e] && col < p.N && qb < p.nq) {
+          const int srow = so_prefix[u.e] + wrow / p.tile_m;
+          cp_async4(s_qa, p.qa + static_cast<int64_t>(srow) * p.q_stride + qb);
+          cp_async4(s_qb, p.qb + (static_cast<int64_t>(u.e) * p.nsb + col / 64) * p.q_stride + qb);
+          any = true;
+        }
       }
-      tc_fence_after();
-      tmem_ld8(tmem_base + t_col + acc * BN, P0);
-      for (int qb = 0; qb < p.nq && ok; ++qb) {
-        const int qa0 = q0, qa1 = q1;
+      if (!any) {
+        st_s32(s_qa, 0);
+        st_s32(s_qb, 0);
+      }
+    };
+    auto take_q = [&](int par) {
+      cp_async_wait_all();
+      const uint32_t s_qa = s_slot + (2 * par) * kSA;
+      return ld_s32(s_qa) * ld_s32(s_qa + kSA);
+    };
+    fetch_q(blockIdx.x, 0);
+    int par = 0;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, par ^= 1) {
+      int qv = take_q(par);
+      fetch_q(t + gridDim.x, par ^ 1);
+      {
+        // F_A, F_B of this tile (needed only by the output phase)
+        const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+        const int wrow0 = ti.mt * BM + quad * 32;
+        const int col0 = ti.nt * BN + cq * 64;
+        if (MODE == kHybrid && wrow0 < m_rows[ti.e] && col0 < p.N) {
+          const int srow = so_prefix[ti.e] + wrow0 / p.tile_m;
+          cp_async4(s_fa, p.fa + static_cast<int64_t>(srow) * p.f_stride);
+          cp_async4(s_fb, p.fb + (static_cast<int64_t>(ti.e) * p.nsb + col0 / 64) * p.f_stride);
+        }
+      }
+      int32_t W[64];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint32_t(&cur)[8] = (c & 1) ? P1 : P0;
-          uint32_t(&nxt)[8] = (c & 1) ? P0 : P1;
-          tmem_wait_ld(cur);
-          if (c < 15) {
-            tmem_ld8(tmem_base + t_col + acc * BN + 8 * (c + 1), nxt);
-          } else {
+      for (int i = 0; i < 64; ++i) W[i] = 0;
+      // One 16-column chunk in flight per warp: with four epilogue warps on
+      // each SM sub-partition the other warps' multiply-adds cover the TMEM
+      // load latency, and the single buffer keeps W[64] in registers.  The
+      // accumulator buffer goes back to the MMA warp as soon as its last
+      // chunk has landed.
+      uint32_t P[16];
+      for (int qb = 0; qb < p.nq && ok; ++qb) {
+        const int q = __shfl_sync(0xffffffffu, qv, qb & 31);
+        if ((qb & 31) == 31 && qb + 1 < p.nq) qv = tile_q(t, qb + 1);  // K > 4096
+        if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm, kErrEpilogueTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld16(tmem_base + t_col + acc * BN + 16 * c, P);
+          tmem_wait_ld(P);
+          if (c == 3) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_acce + 8 * acc);
             if (++acc == NACC) acc = 0, aphase ^= 1;
-            if (qb + 1 < p.nq) {
-              qfac(qb + 1, q0, q1);
-              if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm,
-                             kErrEpilogueTimeout)) {
-                ok = false;
-              } else {
-                tc_fence_after();
-                tmem_ld8(tmem_base + t_col + acc * BN, nxt);
-              }
-            }
           }
-          const int q = (c < 8) ? qa0 : qa1;
           if (MODE == kHybrid) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) W[8 * c + i] += q * static_cast<int32_t>(cur[i]);
+            for (int i = 0; i < 16; ++i) W[16 * c + i] += q * static_cast<int32_t>(P[i]);
           } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) W[8 * c + i] += static_cast<int32_t>(cur[i]);
+            for (int i = 0; i < 16; ++i) W[16 * c + i] += static_cast<int32_t>(P[i]);
           }
         }
       }
       if (!ok) break;
-      // ---- convert, scale, round, store (direct 16-B stores of the row) ----
-      float f0, f1;
+      // ---- convert, scale, round, store ----
+      const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+      const int m_e = m_rows[ti.e];
+      const int wrow0 = ti.mt * BM + quad * 32;
+      const int lrow = wrow0 + lane;
+      const int col0 = ti.nt * BN + cq * 64;
+      float f;
       if (MODE == kHybrid) {
-        const float fa = row_ok ? __ldg(p.fa + static_cast<int64_t>(srow) * p.f_stride) : 0.f;
-        const float* fbp = p.fb + (static_cast<int64_t>(ti.e) * p.nsb + jb) * p.f_stride;
-        f0 = c0_ok ? fa * __ldg(fbp) : 0.f;
-        f1 = c1_ok ? fa * __ldg(fbp + p.f_stride) : 0.f;
+        cp_async_wait_all();
+        f = __int_as_float(ld_s32(s_fa)) * __int_as_float(ld_s32(s_fb));
       } else if (p.a_row_scale != nullptr) {
-        const int grow = __ldg(p.eo + ti.e) + (row_ok ? lrow : 0);
-        f0 = f1 = __ldg(p.a_row_scale + grow) * __ldg(p.b_expert_scale + ti.e);
+        f = lrow < m_e ? __ldg(p.a_row_scale + e_row0[ti.e] + lrow) * __ldg(p.b_expert_scale + ti.e)
+                       : 0.f;
       } else {
-        f0 = f1 = p.alpha;
+        f = p.alpha;
       }
-      if (!(row_ok && c0_ok)) continue;
-      const int ncols = min(128, p.N - col0);
-      const int64_t row_off = static_cast<int64_t>(__ldg(p.eo + ti.e) + lrow) * p.N + col0;
+      if constexpr (!std::is_same<OutT, int32_t>::value) {
+        if (wrow0 + 32 <= m_e && col0 + 64 <= p.N) {
+          // All 32 rows belong to this expert: stage the warp's 32 x 64 block
+          // in shared memory (64-byte swizzle, conflict-free) and write it
+          // with two TMA tensor stores of 32 x 32, so the stores leave as
+          // whole lines instead of 32 row fragments per instruction.
+          const uint32_t stg = sbase + SmemLayout::kStg + (warp - 2) * SmemLayout::kStgWarpBytes;
+          const float* bp =
+              HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0 : nullptr;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (lane == 0) bulk_wait_read0();  // the previous store has read the buffer
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t w4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int c = 32 * h + 8 * j + 2 * i;
+                if (HAS_BIAS) {
+                  w4[i] = pack2<OutT>(fmaf(static_cast<float>(W[c]), f, __ldg(bp + c)),
+                                      fmaf(static_cast<float>(W[c + 1]), f, __ldg(bp + c + 1)));
+                } else {
+                  w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[c]), f),
+                                      __fmul_rn(static_cast<float>(W[c + 1]), f));
+                }
+              }
+              const uint32_t a = stg + 64 * lane + 16 * (j ^ ((lane >> 1) & 3));
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w4[0]),
+                           "r"(w4[1]), "r"(w4[2]), "r"(w4[3])
+                           : "memory");
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmO, stg, col0 + 32 * h, e_row0[ti.e] + wrow0);
+              bulk_commit();
+            }
+          }
+          continue;
+        }
+      }
+      if (!(lrow < m_e && col0 < p.N)) continue;
+      const int64_t row_off = static_cast<int64_t>(e_row0[ti.e] + lrow) * p.N + col0;
+      const int ncols = min(64, p.N - col0);
       if constexpr (std::is_same<OutT, int32_t>::value) {
         // raw accumulator output (verification mode)
         int32_t* dst = static_cast<int32_t*>(p.out) + row_off;
+        (void)f;
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
+        for (int c = 0; c < 16; ++c)
           if (4 * c < ncols)
             *reinterpret_cast<int4*>(dst + 4 * c) =
                 make_int4(W[4 * c], W[4 * c + 1], W[4 * c + 2], W[4 * c + 3]);
-        (void)f0;
-        (void)f1;
       } else {
         OutT* dst = static_cast<OutT*>(p.out) + row_off;
         const float* bp = HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0
                                    : nullptr;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
+        for (int c = 0; c < 8; ++c) {
           if (8 * c >= ncols) continue;
-          const float f = (c < 8) ? f0 : f1;
           uint32_t w4[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -488,6 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    cp_async_wait_all();  // no asynchronous copy into shared memory outlives the CTA
+    if (lane == 0) bulk_wait0();  // nor a tensor store still reading the staging buffer
   }
 
   tc_fence_before();
@@ -548,9 +666,23 @@ int make_tmap_b(CUtensorMap* m, const int8_t* b, int64_t E, int64_t n, int64_t k
   return I8MOE_OK;
 }
 
+int make_tmap_out(CUtensorMap* m, void* out, int out_dtype, int64_t rows, int64_t n) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(n * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t es[2] = {1, 1};
+  const CUtensorMapDataType dt = out_dtype == I8MOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = g_encode(m, dt, 2, out, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(I8MOE_ERR_CUDA, "cuTensorMapEncodeTiled(out) failed");
+  return I8MOE_OK;
+}
+
 template <int MODE, bool HAS_BIAS, typename OutT>
-int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
-             cudaStream_t st) {
+int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+             const GemmParams& p, int grid, cudaStream_t st) {
   auto kern = grouped_gemm_kernel<MODE, HAS_BIAS, OutT>;
   const int smem = SmemLayout::bytes(p.E) + 1024;
   static int attr_done[64] = {0};
@@ -560,7 +692,7 @@ int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, 
                                  SmemLayout::bytes(kMaxExperts) + 1024));
     if (dev >= 0 && dev < 64) __atomic_store_n(&attr_done[dev], 1, __ATOMIC_RELEASE);
   }
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, to, p);
   return check_launch("grouped_gemm_kernel");
 }
 
@@ -597,6 +729,11 @@ int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const i
   if (rc) return rc;
   rc = make_tmap_b(&tb, b, E, n, k);
   if (rc) return rc;
+  CUtensorMap to = ta;  // the raw int32 output is written without a tensor map
+  if (out_dtype != I8MOE_S32) {
+    rc = make_tmap_out(&to, p.out, out_dtype, sum_m, n);
+    if (rc) return rc;
+  }
   p.E = static_cast<int>(E);
   p.sum_m = static_cast<int>(sum_m);
   p.N = static_cast<int>(n);
@@ -612,18 +749,18 @@ int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const i
   const int grid = static_cast<int>(std::min<int64_t>(num_sms(current_device()), upper_tiles));
   if (out_dtype == I8MOE_S32) {
     I8_REQUIRE(!has_bias, "the raw int32 accumulator output takes no bias");
-    return mode == kHybrid ? launch_t<kHybrid, false, int32_t>(ta, tb, p, grid, st)
-                           : launch_t<kPerTensor, false, int32_t>(ta, tb, p, grid, st);
+    return mode == kHybrid ? launch_t<kHybrid, false, int32_t>(ta, tb, to, p, grid, st)
+                           : launch_t<kPerTensor, false, int32_t>(ta, tb, to, p, grid, st);
   }
   if (mode == kHybrid) {
     if (out_dtype == I8MOE_BF16)
-      return has_bias ? launch_t<kHybrid, true, __nv_bfloat16>(ta, tb, p, grid, st)
-                      : launch_t<kHybrid, false, __nv_bfloat16>(ta, tb, p, grid, st);
-    return has_bias ? launch_t<kHybrid, true, __half>(ta, tb, p, grid, st)
-                    : launch_t<kHybrid, false, __half>(ta, tb, p, grid, st);
+      return has_bias ? launch_t<kHybrid, true, __nv_bfloat16>(ta, tb, to, p, grid, st)
+                      : launch_t<kHybrid, false, __nv_bfloat16>(ta, tb, to, p, grid, st);
+    return has_bias ? launch_t<kHybrid, true, __half>(ta, tb, to, p, grid, st)
+                    : launch_t<kHybrid, false, __half>(ta, tb, to, p, grid, st);
   }
-  if (out_dtype == I8MOE_BF16) return launch_t<kPerTensor, false, __nv_bfloat16>(ta, tb, p, grid, st);
-  return launch_t<kPerTensor, false, __half>(ta, tb, p, grid, st);
+  if (out_dtype == I8MOE_BF16) return launch_t<kPerTensor, false, __nv_bfloat16>(ta, tb, to, p, grid, st);
+  return launch_t<kPerTensor, false, __half>(ta, tb, to, p, grid, st);
 }
 
 }  // namespace
