@@ -5,7 +5,7 @@ Importing the package loads libi8moe.so (``INT8_HYBRID_MOE_LIB`` overrides
 the in-tree path) and registers the reference's operator namespace
 ``torch.ops.int8_hybrid_moe``.  The Python modules mirror the reference's
 ``int8_hybrid_moe`` package: ``ops``, ``permute``, ``quant``, ``activation``
-and ``cutlass_runner``; ``ep`` adds expert parallelism over NCCL.
+and ``cutlass_runner``.
 """
 
 from . import _lib  # noqa: F401  (loads the shared library, raises if missing)
