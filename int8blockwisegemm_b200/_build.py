@@ -1,6 +1,6 @@
 """Build libi8moe.so in-tree with nvcc for sm_100a.
 
-    python -m int8blockwisegemm_b200._build [--force] [--verbose]
+    python int8blockwisegemm_b200/_build.py [--force] [--verbose]
 
 Objects go to int8blockwisegemm_b200/_build/ (git-ignored); the shared
 library is written next to this file so it travels with the source tree.

@@ -53,7 +53,7 @@ def _load():
     if not os.path.isfile(LIB_PATH):
         raise RuntimeError(
             f"Cannot find libi8moe.so at {LIB_PATH}.\n"
-            "Build it first:  python -m int8blockwisegemm_b200._build\n"
+            "Build it first:  python int8blockwisegemm_b200/_build.py\n"
             "or set INT8_HYBRID_MOE_LIB to the path of the compiled .so.")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in PROTOTYPES.items():

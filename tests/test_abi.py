@@ -1,0 +1,58 @@
+"""The C ABI without a GPU: libi8moe.so loads, exports every function that
+include/i8moe.h declares with the prototype table the bindings use, and the
+argument checks that run before any CUDA call return their documented codes."""
+
+import ctypes
+import re
+
+import pytest
+
+from tests.conftest import ROOT
+
+HEADER = ROOT / "include" / "i8moe.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)  # drop comments
+    return sorted(set(re.findall(r"\b(i8moe_\w+)\s*\(", text)))
+
+
+def test_header_declares_functions():
+    names = header_functions()
+    assert "i8moe_hybrid_grouped_gemm" in names and len(names) >= 15
+
+
+def test_library_exports_every_header_function():
+    from int8blockwisegemm_b200 import _lib
+    names = [n for n in header_functions() if n != "i8moe_moe_permute_metadata_noalloc"]
+    missing_proto = [n for n in names if n not in _lib.PROTOTYPES]
+    assert not missing_proto, f"no ctypes prototype for {missing_proto}"
+    extra_proto = [n for n in _lib.PROTOTYPES if n not in header_functions()]
+    assert not extra_proto, f"prototypes for undeclared functions {extra_proto}"
+    raw = ctypes.CDLL(_lib.LIB_PATH)
+    for n in names:
+        assert hasattr(raw, n), f"libi8moe.so does not export {n}"
+
+
+def test_calls_that_need_no_gpu():
+    from int8blockwisegemm_b200 import _lib
+    lib = _lib.LIB
+    assert lib.i8moe_abi_version() >= 1
+    assert lib.i8moe_moe_permute_unpermute_supported() == 1
+    # 2048-key chunks x 2^bits buckets x 4 bytes
+    assert lib.i8moe_route_workspace_size(65536, 256) == 32 * 512 * 4
+    assert lib.i8moe_route_workspace_size(1, 8) == 1 * 16 * 4
+    assert lib.i8moe_route_workspace_size(10, 0) == 0
+
+
+def test_argument_errors_before_any_cuda_call():
+    from int8blockwisegemm_b200 import _lib
+    lib = _lib.LIB
+    rc = lib.i8moe_moe_permute_metadata(None, None, None, 4, 2, 0, 0, None, None, None, None, 0,
+                                        None)
+    assert rc == -1 and "n_expert" in _lib.last_error()
+    rc = lib.i8moe_moe_permute_metadata(None, None, None, 4, 2, 8, 8, None, None, None, None, 0,
+                                        None)
+    assert rc == -1 and "workspace" in _lib.last_error()
+
