@@ -76,6 +76,25 @@ int i8moe_moe_permute_metadata(const int32_t* topk_ids, const int32_t* token_exp
                                int32_t* permuted_idx, void* workspace, size_t workspace_bytes,
                                i8moe_stream_t stream);
 
+/* No reference counterpart.  moe_permute_metadata for callers that cannot
+ * allocate device memory per call: identical arguments and results to
+ * i8moe_moe_permute_metadata minus the workspace, whose role is taken by a
+ * fixed 1 MiB device array inside the library (so it needs
+ * i8moe_route_workspace_size(n_token*topk, n_expert) <= 1048576 bytes, e.g.
+ * up to 1,048,576 rows at 256 experts; larger problems return
+ * I8MOE_ERR_INVALID and must use the workspace entry point).  The first call
+ * on a device looks the array up with cudaGetSymbolAddress, so make it before
+ * any stream capture on that device.  The array is shared by every call on a
+ * device: calls that overlap on one device race and must be serialised by the
+ * caller.  Nothing is allocated. */
+int i8moe_moe_permute_metadata_noalloc(const int32_t* topk_ids,
+                                       const int32_t* token_expert_indices,
+                                       const int32_t* expert_map, int64_t n_token, int64_t topk,
+                                       int64_t n_expert, int64_t n_local_expert,
+                                       int64_t* expert_first_token_offset,
+                                       int32_t* inv_permuted_idx, int32_t* permuted_idx,
+                                       i8moe_stream_t stream);
+
 /* Fused-forward variant of i8moe_moe_permute_metadata (no reference
  * counterpart; it replaces the host-side torch glue of the reference runner,
  * int8_hybrid_moe/cutlass_runner.py:136-143 and the scale-offset cumsum of

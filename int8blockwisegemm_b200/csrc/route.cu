@@ -17,6 +17,7 @@
 // A stable counting sort on the same bits yields exactly the order of the
 // stable LSD radix sort, so the maps are bit-identical.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -438,6 +439,72 @@ int launch_route_fused(const int32_t* topk_ids, const int32_t* tei, const int32_
                       ws_bytes, st, fx);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free routing scratch
+// ---------------------------------------------------------------------------
+// Some callers cannot hand the routing kernels a workspace: they run without a
+// caching allocator, inside a pre-sized arena, or in a loop where allocating
+// device memory per call is not allowed.  For them the per-chunk histogram
+// lives in a fixed device array compiled into this library.  Its size caps the
+// problem (buckets x 2048-key chunks x 4 bytes); anything larger must use the
+// workspace entry point.  The histogram kernel writes every slot it later
+// reads, so nothing in the array has to start at zero.  There is one array per
+// device, so two calls that overlap on one device (two streams, two threads)
+// would race on it: calls on a device must be serialised.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;  // 1 MiB
+static __device__ __align__(256) unsigned char g_route_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxScratchDevices = 64;
+struct ScratchSlot {
+  std::once_flag once;
+  void* ptr = nullptr;
+  cudaError_t status = cudaSuccess;
+};
+ScratchSlot g_scratch_slots[kMaxScratchDevices];
+
+// Device address of g_route_scratch on the current device, looked up once per
+// device (with that device current) and cached.
+int route_scratch_ptr(void** out) {
+  int dev = -1;
+  I8_CUDA(cudaGetDevice(&dev));
+  I8_REQUIRE(dev >= 0 && dev < kMaxScratchDevices,
+             "moe_permute_metadata_noalloc: device ordinal %d out of range", dev);
+  ScratchSlot& slot = g_scratch_slots[dev];
+  std::call_once(slot.once, [&slot] {
+    void* p = nullptr;
+    slot.status = cudaGetSymbolAddress(&p, g_route_scratch);
+    if (slot.status == cudaSuccess) slot.ptr = p;
+  });
+  if (slot.status != cudaSuccess)
+    return set_error(I8MOE_ERR_CUDA, std::string("cudaGetSymbolAddress(route scratch): ") +
+                                         cudaGetErrorString(slot.status));
+  *out = slot.ptr;
+  return I8MOE_OK;
+}
+
+}  // namespace
+
+int launch_route_noalloc(const int32_t* topk_ids, const int32_t* tei, const int32_t* emap,
+                         int64_t n_token, int64_t topk, int64_t n_expert, int64_t n_local,
+                         int64_t* eft, int32_t* inv, int32_t* pidx, cudaStream_t st) {
+  I8_REQUIRE(n_token >= 0 && topk > 0, "moe_permute: bad n_token/topk");
+  I8_REQUIRE(n_expert >= 1 && n_expert <= 2048, "moe_permute: n_expert must be in [1, 2048]");
+  const size_t need = route_ws_bytes(n_token * topk, n_expert);
+  I8_REQUIRE(need <= kNoAllocScratchBytes,
+             "moe_permute_metadata_noalloc: %lld rows of %lld experts need %zu bytes of routing "
+             "scratch, more than the fixed %zu-byte device buffer; use "
+             "i8moe_moe_permute_metadata with a caller workspace",
+             static_cast<long long>(n_token * topk), static_cast<long long>(n_expert), need,
+             kNoAllocScratchBytes);
+  void* ws = nullptr;
+  const int rc = route_scratch_ptr(&ws);
+  if (rc) return rc;
+  return launch_route(topk_ids, tei, emap, n_token, topk, n_expert, n_local, eft, inv, pidx, ws,
+                      kNoAllocScratchBytes, st, FusedExtras{});
+}
+
 }  // namespace i8moe
 
 using namespace i8moe;
@@ -461,6 +528,18 @@ int i8moe_moe_permute_metadata(const int32_t* topk_ids, const int32_t* token_exp
                       n_local_expert, expert_first_token_offset, inv_permuted_idx, permuted_idx,
                       workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                       FusedExtras{});
+}
+
+int i8moe_moe_permute_metadata_noalloc(const int32_t* topk_ids,
+                                       const int32_t* token_expert_indices,
+                                       const int32_t* expert_map, int64_t n_token, int64_t topk,
+                                       int64_t n_expert, int64_t n_local_expert,
+                                       int64_t* expert_first_token_offset,
+                                       int32_t* inv_permuted_idx, int32_t* permuted_idx,
+                                       i8moe_stream_t stream) {
+  return launch_route_noalloc(topk_ids, token_expert_indices, expert_map, n_token, topk, n_expert,
+                              n_local_expert, expert_first_token_offset, inv_permuted_idx,
+                              permuted_idx, static_cast<cudaStream_t>(stream));
 }
 
 int i8moe_moe_route_for_gemm(const int32_t* topk_ids, const int32_t* token_expert_indices,

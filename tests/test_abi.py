@@ -25,10 +25,10 @@ def test_header_declares_functions():
 
 def test_library_exports_every_header_function():
     from int8blockwisegemm_b200 import _lib
-    names = [n for n in header_functions() if n != "i8moe_moe_permute_metadata_noalloc"]
+    names = header_functions()
     missing_proto = [n for n in names if n not in _lib.PROTOTYPES]
     assert not missing_proto, f"no ctypes prototype for {missing_proto}"
-    extra_proto = [n for n in _lib.PROTOTYPES if n not in header_functions()]
+    extra_proto = [n for n in _lib.PROTOTYPES if n not in names]
     assert not extra_proto, f"prototypes for undeclared functions {extra_proto}"
     raw = ctypes.CDLL(_lib.LIB_PATH)
     for n in names:
@@ -56,3 +56,13 @@ def test_argument_errors_before_any_cuda_call():
                                         None)
     assert rc == -1 and "workspace" in _lib.last_error()
 
+
+def test_noalloc_rejects_problems_above_its_fixed_scratch():
+    from int8blockwisegemm_b200 import _lib
+    lib = _lib.LIB
+    # 2048 experts -> 4096 buckets x 16 KiB per chunk: 128 chunks fill 2 MiB
+    rc = lib.i8moe_moe_permute_metadata_noalloc(None, None, None, 32768, 8, 2048, 2048, None,
+                                                None, None, None)
+    assert rc == -1
+    msg = _lib.last_error()
+    assert "fixed" in msg and "i8moe_moe_permute_metadata" in msg
