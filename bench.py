@@ -15,9 +15,13 @@ entry point (cutlass_runner._run_cutlass_int8_hybrid_grouped_moe) called
 eagerly with the per-step inputs copied from pinned host memory and the
 output copied back inside the timed region.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own batch of
-the configuration (data-parallel replicas, weak scaling); the timed region is
-bracketed by barriers and the reported time is the max over ranks.
+Multi-GPU (torchrun, one process per GPU): expert parallelism.  Rank r owns
+experts [r*E/N, (r+1)*E/N) and the configuration's T tokens of its own
+(global batch N*T, weak scaling); a step is one NCCL dispatch all-to-all, the
+local forward of the rows that reached the rank, and one combine all-to-all.
+The dispatch sizes its payload exchange from host-side counts, so EP steps
+run eagerly (no CUDA graph).  The timed region is bracketed by barriers and
+the reported time is the max over ranks.
 
 ``--impl reference`` times the CPU restatement of the reference path
 (oracle/ref_cpu.py, numpy on the host cores) on a bounded token sample of the
@@ -292,7 +296,134 @@ def time_w13_gemm(pkg, cfg, st, tr, iters=20):
     return e0.elapsed_time(e1) / iters * 1e-3
 
 
+def run_ours_ep(args, world, rank, local):
+    """Expert-parallel forward over ``world`` GPUs (NCCL all-to-all)."""
+    from dataclasses import replace
+    import int8blockwisegemm_b200 as pkg
+    from int8blockwisegemm_b200.ep import EPMoE, ExpertParallel, global_tile_m
+    wl = load_workloads()
+    cfg = wl.CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    gcfg = replace(cfg, T=cfg.T * world)     # weak scaling: cfg.T tokens per rank
+    inp = wl.make_inputs(gcfg)               # the same global inputs on every rank
+    r = pkg.cutlass_runner
+    r._USE_FUSED_PERMUTE_QUANT_W1 = True
+    r._USE_FUSED_SILU_QUANT_W2 = True
+    T, k = cfg.T, cfg.topk
+    sl = slice(rank * T, (rank + 1) * T)
+    ep = ExpertParallel(cfg.E)
+    tm = global_tile_m(gcfg.T, k, cfg.E)
+    moe = EPMoE(ep, inp["w13"].to(dev), inp["w2"].to(dev), inp["w13_q"].to(dev),
+                inp["w13_f"].to(dev), inp["w2_q"].to(dev), inp["w2_f"].to(dev),
+                quant_block_size=cfg.quant_block, super_group_size=cfg.sg, q_max=cfg.q_max,
+                tile_m=tm)
+    hidden = inp["hidden"][sl].to(dev)
+    ids = inp["topk_ids"][sl].to(dev)
+    wts = inp["topk_weights"][sl].to(dev)
+    out = torch.empty_like(hidden)
+    ops_per_step = 2 * T * k * (2 * cfg.N) * cfg.K + 2 * T * k * cfg.K * cfg.N
+
+    if args.profile_steps:
+        for _ in range(args.profile_steps):
+            moe.forward(hidden, ids, wts, out)
+        torch.cuda.synchronize()
+        return
+
+    for _ in range(max(3, args.warmup)):
+        moe.forward(hidden, ids, wts, out)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(args.steps):
+            moe.forward(hidden, ids, wts, out)
+        e1.record(s)
+        torch.cuda.synchronize()
+        barrier(world)
+    dt = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    clocks = clk.summary()
+
+    e2e = None
+    if not args.no_e2e:
+        h_hidden, h_ids, h_w = (inp["hidden"][sl].pin_memory(), inp["topk_ids"][sl].pin_memory(),
+                                inp["topk_weights"][sl].pin_memory())
+        h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        d_hidden, d_ids, d_w = torch.empty_like(hidden), torch.empty_like(ids), torch.empty_like(wts)
+
+        def e2e_step():
+            d_hidden.copy_(h_hidden, non_blocking=True)
+            d_ids.copy_(h_ids, non_blocking=True)
+            d_w.copy_(h_w, non_blocking=True)
+            moe.forward(d_hidden, d_ids, d_w, out)
+            h_out.copy_(out, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        barrier(world)
+        dte = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+        bi = h_hidden.numel() * h_hidden.element_size() + h_ids.numel() * 4 + h_w.numel() * 4
+        e2e = {"value": world * ops_per_step * args.steps / dte / 1e12, "unit": "TOPS",
+               "ms_per_step": dte / args.steps * 1e3, "h2d_bytes_per_step": bi,
+               "d2h_bytes_per_step": h_out.numel() * h_out.element_size()}
+
+    # roofline: this rank's local w13 GEMM, timed like the single-GPU one
+    tr = {}
+    moe.forward(hidden, ids, wts, out, trace=tr)
+    torch.cuda.synchronize()
+    R_buf = tr["a1q"].shape[0]
+    st = {"w1": moe.w1, "w1_qscale": moe.w1_q, "w1_fscale": moe.w1_f,
+          "workspace13": torch.empty(R_buf * 2 * cfg.N, dtype=hidden.dtype, device=dev)}
+    t_gemm = max_over_ranks(time_w13_gemm(pkg, cfg, st, tr), world)
+    eft = tr["eft"].cpu()
+    R_loc = int(eft[-1])
+    e_hit = int(((eft[1:] - eft[:-1]) > 0).sum())
+    n_sb, kb = -(-2 * cfg.N // 64), -(-cfg.K // 128)
+    gemm_bytes = (R_loc * cfg.K + e_hit * 2 * cfg.N * cfg.K + R_loc * 2 * cfg.N * 2
+                  + e_hit * n_sb * kb * 4 * 2 + tr["a1_Q"].shape[0] * kb * 4)
+    hbm, _, src = measured_peaks()
+    achieved = gemm_bytes / t_gemm / 1e9
+    line = {
+        "metric": METRIC, "value": world * ops_per_step * args.steps / dt / 1e12, "unit": "TOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: T={cfg.T} tokens per rank (global {gcfg.T}),"
+                               f"K={cfg.K},N={cfg.N},E={cfg.E},top{k},{cfg.dtype} activations, "
+                               f"fused permute+quant and SiLU+quant",
+                   "parallelism": f"ep{world}: experts split contiguously, NCCL all-to-all "
+                                  "dispatch and combine",
+                   "global_batch_tokens": gcfg.T,
+                   "l2": "no flush: weights+activations exceed the 126 MB L2",
+                   "timing": "eager EP forward (dispatch sizes come from host-side counts), "
+                             "CUDA events, max over ranks"},
+        "clocks": clocks,
+        "gpu_launches": 8 * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel (w13, local experts)",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": src, "traffic": None, "algorithmic_bytes": gemm_bytes,
+                     "launch_ms": t_gemm * 1e3,
+                     "int8_tops": 2 * R_loc * 2 * cfg.N * cfg.K / t_gemm / 1e12},
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
+    if world > 1:
+        return run_ours_ep(args, world, rank, local)
     wl = load_workloads()
     cfg = wl.CONFIGS[args.config]
     dev = torch.device("cuda", local)

@@ -78,11 +78,16 @@ def _run_cutlass_int8_hybrid_grouped_moe(
     q_max: int,
     *,
     _trace: dict | None = None,
+    _tile_m: int | None = None,
 ) -> None:
     """Full INT8 hybrid grouped MoE forward; writes ``output`` [M, K].
 
-    ``_trace`` (keyword-only, not in the reference signature): when a dict is
-    given, every intermediate tensor is stored in it for verification."""
+    Keyword-only additions to the reference signature:
+    ``_trace``: when a dict is given, every intermediate tensor is stored in
+    it for verification.
+    ``_tile_m``: forces the quant tile height (64 or 128) instead of the
+    rows-per-expert rule; expert parallelism passes the single-GPU choice so
+    its quant tiles match a single-GPU run."""
     assert activation.is_gated, "Only gated activation is supported"
     assert hidden_states.dtype in (torch.float16, torch.bfloat16, torch.float32)
     assert w1.dtype == torch.int8 and w2.dtype == torch.int8
@@ -104,6 +109,8 @@ def _run_cutlass_int8_hybrid_grouped_moe(
     num_expert = global_num_experts if expert_map is None else expert_map.size(0)
 
     variant = pick_grouped_hybrid_variant(sum_M, local_E)
+    if _tile_m is not None:
+        variant = {128: "hybrid", 64: "hybrid_small"}[_tile_m]
     tile_m = _variant_tile_m(variant)
     gemm = _dispatch_grouped_hybrid(variant)
 

@@ -1,0 +1,183 @@
+"""Expert parallelism for the INT8 hybrid MoE forward over torch.distributed.
+
+The experts are split contiguously: rank r owns experts
+[r*E/P, (r+1)*E/P).  Each rank holds a contiguous shard of the tokens.  A
+forward is one dispatch all-to-all, the unchanged single-GPU forward over the
+rows that reached this rank (restricted to its local experts by an
+``expert_map``, as the reference runner supports), and one combine
+all-to-all:
+
+* dispatch: every token row travels once to every rank that owns at least one
+  of its top-k experts, together with its top-k ids and weights.  Segments
+  are ordered by source rank and, within one, by token index, so the rows a
+  rank receives are in global token order.  The stable per-expert sort of the
+  local routing then puts every expert's rows in the same order as a
+  single-GPU run.  With the tile_m of the single-GPU run (chosen from the
+  global rows per expert) the INT8 activation tiles, scales, int32
+  accumulators and mm1/mm2 rows of each expert are therefore bit-identical
+  to the single-GPU forward.
+* local forward: the top-k weighted unpermute sums this rank's experts of
+  each received token (fp32 in top-k order, then the storage type).
+* combine: the partial rows return to their source ranks, which add them in
+  fp32 in rank order (one segment per rank, so the order is deterministic)
+  and round once.  Only this summation order differs from one GPU, so the
+  output agrees within the reference's tolerance rather than bit for bit.
+
+The all-to-alls are ``torch.distributed.all_to_all_single`` calls (NCCL over
+NVLink/NVSwitch on GPUs; gloo for the CPU tests).  Counts travel first; their
+host copy fixes the split sizes of the payload exchange, so a forward
+synchronises with the host once per dispatch.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class Dispatched:
+    """Rows this rank received and what the combine needs to send them back."""
+    hidden: torch.Tensor        # [n_recv, K]
+    topk_ids: torch.Tensor      # [n_recv, k] int32, global expert ids
+    topk_weights: torch.Tensor  # [n_recv, k] float32
+    send_idx: torch.Tensor      # [n_send] int64 local token index of every sent row
+    send_counts: list[int]      # rows sent to each rank
+    recv_counts: list[int]      # rows received from each rank
+    n_token: int                # local tokens
+
+
+class ExpertParallel:
+    """Dispatch / combine for ``num_experts`` experts over ``group``."""
+
+    def __init__(self, num_experts: int, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if num_experts % self.world != 0:
+            raise ValueError(f"num_experts={num_experts} is not divisible by the "
+                             f"{self.world} ranks of the group")
+        self.num_experts = num_experts
+        self.n_local = num_experts // self.world
+        self.first = self.rank * self.n_local
+
+    def expert_map(self, device) -> torch.Tensor:
+        """global expert id -> local id, -1 for experts of other ranks."""
+        m = torch.full((self.num_experts,), -1, dtype=torch.int32)
+        m[self.first:self.first + self.n_local] = torch.arange(self.n_local, dtype=torch.int32)
+        return m.to(device)
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
+        dist.all_to_all_single(out, inp, output_split_sizes=list(out_splits),
+                               input_split_sizes=list(in_splits), group=self.group)
+
+    def dispatch(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
+                 topk_weights: torch.Tensor) -> Dispatched:
+        T, k = topk_ids.shape
+        dev = hidden.device
+        dest = topk_ids.long() // self.n_local                       # [T, k]
+        member = torch.zeros(T, self.world, dtype=torch.bool, device=dev)
+        member.scatter_(1, dest.clamp(0, self.world - 1), True)
+        # rows for rank d: the tokens with an expert on d, in token order
+        order = member.t().nonzero()                                 # [n_send, 2] (rank, token)
+        send_idx = order[:, 1]
+        counts = member.sum(0).to(torch.int64)                       # [P]
+        recv = torch.empty_like(counts)
+        self._a2a(recv, counts, [1] * self.world, [1] * self.world)
+        send_counts = counts.cpu().tolist()
+        recv_counts = recv.cpu().tolist()
+        n_recv = sum(recv_counts)
+        r_hidden = torch.empty(n_recv, hidden.shape[1], dtype=hidden.dtype, device=dev)
+        r_ids = torch.empty(n_recv, k, dtype=torch.int32, device=dev)
+        r_w = torch.empty(n_recv, k, dtype=torch.float32, device=dev)
+        self._a2a(r_hidden, hidden.index_select(0, send_idx).contiguous(), recv_counts,
+                  send_counts)
+        self._a2a(r_ids, topk_ids.to(torch.int32).index_select(0, send_idx).contiguous(),
+                  recv_counts, send_counts)
+        self._a2a(r_w, topk_weights.to(torch.float32).index_select(0, send_idx).contiguous(),
+                  recv_counts, send_counts)
+        return Dispatched(r_hidden, r_ids, r_w, send_idx, send_counts, recv_counts, T)
+
+    def combine(self, d: Dispatched, partial: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """Return the partial rows to their sources and sum them per token."""
+        K = partial.shape[1]
+        back = torch.empty(sum(d.send_counts), K, dtype=partial.dtype, device=partial.device)
+        self._a2a(back, partial.contiguous(), d.send_counts, d.recv_counts)
+        acc = torch.zeros(d.n_token, K, dtype=torch.float32, device=partial.device)
+        start = 0
+        for n in d.send_counts:  # each segment holds distinct tokens: a deterministic order
+            if n:
+                acc.index_add_(0, d.send_idx[start:start + n], back[start:start + n].float())
+            start += n
+        if out is None:
+            return acc.to(partial.dtype)
+        out.copy_(acc)
+        return out
+
+    def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                local_forward: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor],
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """dispatch -> ``local_forward(hidden, topk_ids, topk_weights)`` -> combine.
+
+        ``local_forward`` returns the [n_recv, K] partial output of this
+        rank's experts for the received rows."""
+        d = self.dispatch(hidden, topk_ids, topk_weights)
+        partial = local_forward(d.hidden, d.topk_ids, d.topk_weights)
+        return self.combine(d, partial, out)
+
+
+def global_tile_m(n_token_global: int, topk: int, num_experts: int) -> int:
+    """tile_m of the single-GPU run (cutlass_runner.py:43-50 on the global
+    rows per expert), which keeps the EP quant tiles identical to it."""
+    from .cutlass_runner import _variant_tile_m, pick_grouped_hybrid_variant
+    return _variant_tile_m(pick_grouped_hybrid_variant(n_token_global * topk, num_experts))
+
+
+class EPMoE:
+    """Expert-parallel INT8 hybrid MoE forward on the sm_100a kernels.
+
+    Holds this rank's slice of the expert weights (experts
+    [rank*E/P, (rank+1)*E/P)) and runs ``cutlass_runner`` on the rows the
+    dispatch delivers."""
+
+    def __init__(self, ep: ExpertParallel, w1, w2, w1_qscale, w1_fscale, w2_qscale, w2_fscale,
+                 *, quant_block_size: int, super_group_size: int, q_max: int, tile_m: int):
+        lo, n = ep.first, ep.n_local
+        self.ep = ep
+        self.w1, self.w2 = w1[lo:lo + n].contiguous(), w2[lo:lo + n].contiguous()
+        self.w1_q, self.w1_f = w1_qscale[lo:lo + n].contiguous(), w1_fscale[lo:lo + n].contiguous()
+        self.w2_q, self.w2_f = w2_qscale[lo:lo + n].contiguous(), w2_fscale[lo:lo + n].contiguous()
+        self.qbs, self.sg, self.q_max, self.tile_m = quant_block_size, super_group_size, q_max, tile_m
+        self.emap = ep.expert_map(w1.device)
+        self._ws = None
+
+    def _workspaces(self, rows: int, K: int, N: int, dtype, device):
+        need13, need2 = rows * max(2 * N, K), rows * max(N, K)
+        if self._ws is None or self._ws[0].numel() < need13 or self._ws[0].dtype != dtype:
+            self._ws = (torch.empty(need13, dtype=dtype, device=device),
+                        torch.empty(need2, dtype=dtype, device=device))
+        return self._ws[0][:need13].view(rows, -1), self._ws[1][:need2].view(rows, -1)
+
+    def local_forward(self, hidden, topk_ids, topk_weights, trace: dict | None = None):
+        from .activation import MoEActivation
+        from .cutlass_runner import _run_cutlass_int8_hybrid_grouped_moe
+        T, k = topk_ids.shape
+        K, N = hidden.shape[1], self.w2.shape[2]
+        out = torch.empty(T, K, dtype=hidden.dtype, device=hidden.device)
+        if T == 0:
+            return out
+        ws13, ws2 = self._workspaces(T * k, K, N, hidden.dtype, hidden.device)
+        _run_cutlass_int8_hybrid_grouped_moe(
+            out, hidden, self.w1, self.w2, topk_ids, topk_weights, MoEActivation.SILU,
+            self.ep.num_experts, self.emap, self.w1_q, self.w1_f, self.w2_q, self.w2_f,
+            ws13, ws2, self.qbs, self.sg, self.q_max, _trace=trace, _tile_m=self.tile_m)
+        return out
+
+    def forward(self, hidden, topk_ids, topk_weights, out=None, trace: dict | None = None):
+        return self.ep.forward(
+            hidden, topk_ids, topk_weights,
+            lambda h, i, w: self.local_forward(h, i, w, trace), out)

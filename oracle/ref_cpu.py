@@ -562,7 +562,7 @@ def moe_forward(hidden, w1, w2, topk_ids, topk_weights, w1_q, w1_f, w2_q, w2_f, 
                 dtype: str, global_num_experts: int, expert_map=None,
                 quant_block_size: int = 128, super_group_size: int = 256, q_max: int = 16,
                 fuse_permute: bool = True, fuse_silu: bool = True,
-                trace: bool = False):
+                trace: bool = False, tile_m: int | None = None):
     """Full INT8 hybrid MoE forward, cutlass_runner.py:69-236.
 
     Both activation-quant paths (fused permute+quant and permute-then-quant)
@@ -589,7 +589,7 @@ def moe_forward(hidden, w1, w2, topk_ids, topk_weights, w1_q, w1_f, w2_q, w2_f, 
     ps1 = np.stack([counts, np.full(local_e, 2 * N), np.full(local_e, K)], 1)
     ps2 = np.stack([counts, np.full(local_e, K), np.full(local_e, N)], 1)
     variant = pick_grouped_hybrid_variant(R, local_e)
-    tm = VARIANT_TILE_M[variant]
+    tm = VARIANT_TILE_M[variant] if tile_m is None else tile_m  # tile_m: forced (EP tests)
     if fuse_permute:
         a1q, s1, so1 = fused_permute_quant(hidden, pidx, topk, eo, tm)
     else:

@@ -1,0 +1,110 @@
+"""Expert parallelism on two GPUs over NCCL.  Each rank runs the EP forward
+(dispatch all-to-all -> sm_100a forward of its local experts -> combine) and,
+on its own GPU, the single-GPU forward of all tokens; per local expert the
+INT8 activations, mm1, a2q and mm2 rows must be bit-identical, and the
+combined output within the reference tolerance (max-abs-rel 1e-2).  Needs
+two GPUs; skipped otherwise."""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, cfg_name, errq):
+    try:
+        import datetime
+        from dataclasses import replace
+        import torch.distributed as dist
+        import int8blockwisegemm_b200 as pkg
+        from int8blockwisegemm_b200.ep import EPMoE, ExpertParallel, global_tile_m
+        from tests.helpers import load_workloads
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        wl = load_workloads()
+        cfg = wl.CONFIGS[cfg_name]
+        inp = wl.make_inputs(cfg)
+        r = pkg.cutlass_runner
+        r._USE_FUSED_PERMUTE_QUANT_W1 = True
+        r._USE_FUSED_SILU_QUANT_W2 = True
+        T, k = inp["topk_ids"].shape
+        d = {kk: v.to(dev) for kk, v in inp.items()}
+        dt = d["hidden"].dtype
+        # single-GPU reference forward of all tokens, on this rank's GPU
+        full_tr = {}
+        full_out = torch.empty(T, cfg.K, dtype=dt, device=dev)
+        r._run_cutlass_int8_hybrid_grouped_moe(
+            full_out, d["hidden"], d["w13"], d["w2"], d["topk_ids"], d["topk_weights"],
+            pkg.activation.MoEActivation.SILU, cfg.E, None, d["w13_q"], d["w13_f"], d["w2_q"],
+            d["w2_f"], torch.empty(T * k, max(2 * cfg.N, cfg.K), dtype=dt, device=dev),
+            torch.empty(T * k, max(cfg.N, cfg.K), dtype=dt, device=dev), cfg.quant_block,
+            cfg.sg, cfg.q_max, _trace=full_tr)
+        ep = ExpertParallel(cfg.E)
+        moe = EPMoE(ep, d["w13"], d["w2"], d["w13_q"], d["w13_f"], d["w2_q"], d["w2_f"],
+                    quant_block_size=cfg.quant_block, super_group_size=cfg.sg,
+                    q_max=cfg.q_max, tile_m=global_tile_m(T, k, cfg.E))
+        per = T // world
+        sl = slice(rank * per, (rank + 1) * per)
+        tr = {}
+        out = moe.forward(d["hidden"][sl].contiguous(), d["topk_ids"][sl].contiguous(),
+                          d["topk_weights"][sl].contiguous(), trace=tr)
+        torch.cuda.synchronize()
+        ref = full_out[sl].float()
+        rel = ((out.float() - ref).abs().max() / ref.abs().max()).item()
+        assert rel <= 1e-2, f"rank {rank}: EP output max-abs-rel {rel:.3e} > 1e-2"
+        assert tr["tile_m"] == full_tr["tile_m"]
+        leo, feo = tr["eft"].cpu(), full_tr["eft"].cpu()
+        for le in range(ep.n_local):
+            e = ep.first + le
+            a, b = int(leo[le]), int(leo[le + 1])
+            fa, fb = int(feo[e]), int(feo[e + 1])
+            assert b - a == fb - fa, f"expert {e}: {b - a} rows vs {fb - fa}"
+            for name in ("a1q", "mm1", "a2q", "mm2"):
+                assert torch.equal(tr[name][a:b], full_tr[name][fa:fb]), f"{name} of expert {e}"
+        assert pkg._lib.device_error(rank) == 0
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException:
+        errq.put(f"rank {rank}:\n{traceback.format_exc()}")
+        raise
+
+
+@pytest.mark.parametrize("cfg_name", ["mid", "default"])
+def test_ep_two_gpus_matches_single_gpu(cfg_name):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, cfg_name, errq))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not alive, "EP ranks did not finish"
+    assert not errs, "\n".join(errs)
+    assert all(p.exitcode == 0 for p in procs)
