@@ -216,6 +216,27 @@ int i8moe_hybrid_grouped_gemm(const int8_t* a_q, const int32_t* a_qscale, const 
                               int64_t quant_block_size, int64_t super_group_size,
                               int64_t tile_m, i8moe_stream_t stream);
 
+/* No reference counterpart: the w13 hybrid GEMM with the SiLU*up + INT8
+ * requant of the intermediate fused into its epilogue.  It produces exactly
+ * what i8moe_hybrid_grouped_gemm (w13, out_dtype = act_dtype) followed by
+ * i8moe_quant_silu would (reference int8_hybrid_grouped_gemm.cu:218-479 then
+ * quant.py:440-579), without writing the [sum_m, 2N] intermediate.
+ *   w13_q [E, 2N, K] int8 (gate rows 0..N-1, up rows N..2N-1) with its Q/F,
+ *   act_dtype   storage type of the intermediate (I8MOE_BF16 / I8MOE_FP16),
+ *   n_act = N   (a multiple of 32),
+ *   scale_offsets [E+1] int32 (entry E = total scale rows), as written by
+ *               i8moe_moe_route_for_gemm / i8moe_scale_offsets for tile_m,
+ *   act_q [sum_m, N] int8, act_qscale [ceil(sum_m/tile_m)+E, ceil(N/128)]
+ *   int32, act_fscale [same rows, ceil(ceil(N/128)/super_group_size)] fp32. */
+int i8moe_hybrid_grouped_gemm_silu_quant(
+    const int8_t* a_q, const int32_t* a_qscale, const float* a_fscale, int64_t a_scale_rows,
+    const int8_t* w13_q, const int32_t* w13_qscale, const float* w13_fscale,
+    const int32_t* expert_offsets, const int32_t* problem_sizes, const int32_t* scale_offsets,
+    const float* bias, int64_t bias_stride, int act_dtype, int64_t n_expert, int64_t sum_m,
+    int64_t n_act, int64_t k, int64_t quant_block_size, int64_t super_group_size,
+    int64_t tile_m, int64_t q_max, int8_t* act_q, int32_t* act_qscale, float* act_fscale,
+    i8moe_stream_t stream);
+
 /* Replaces cutlass_int8_grouped_mm (csrc/int8_grouped_gemm.cu:106-220,
  * schema csrc/torch_bindings.cpp:75-78):
  *   out[r,n] = out_dtype(float(sum_k a[r,k]*b[e,n,k]) * alpha_r)

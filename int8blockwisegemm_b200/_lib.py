@@ -44,6 +44,9 @@ PROTOTYPES = {
     "i8moe_quantize_scales": (I32, [P, I64, I64, I64, I64, P, P, P]),
     "i8moe_hybrid_grouped_gemm": (I32, [P, P, P, I64, P, P, P, P, P, P, P, I64, P, I32, I64, I64,
                                         I64, I64, I64, I64, I64, P]),
+    "i8moe_hybrid_grouped_gemm_silu_quant": (I32, [P, P, P, I64, P, P, P, P, P, P, P, I64, I32,
+                                                   I64, I64, I64, I64, I64, I64, I64, I64, P, P,
+                                                   P, P]),
     "i8moe_int8_grouped_mm": (I32, [P, P, P, I32, c_float, P, P, P, P, I64, I64, I64, I64, P]),
 }
 

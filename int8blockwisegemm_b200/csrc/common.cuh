@@ -23,6 +23,11 @@ namespace i8moe {
 // host-side status plumbing (capi.cu)
 // ---------------------------------------------------------------------------
 int set_error(int code, const std::string& msg);
+// quant.cu: Q/F factorisation of raw block scales (shared by the fused w13
+// epilogue's entry point)
+int launch_scales_to_qf(const float* scale, int64_t rows_upper, const int32_t* rows_dev,
+                        int64_t kb, int64_t q_max, int64_t sg, int32_t* Q, float* F,
+                        cudaStream_t st);
 int check_launch(const char* what);
 int num_sms(int device);
 int current_device();

@@ -48,6 +48,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "quant_math.cuh"
 
 namespace i8moe {
 
@@ -80,6 +81,9 @@ constexpr uint32_t kTmemCols = NACC * BN;
 constexpr uint32_t kIdesc = idesc_i8(BM, BN);
 
 enum GemmMode { kHybrid = 0, kPerTensor = 1 };
+// Epilogue: store the scaled product, or (w13 only) SiLU(gate)*up + INT8
+// requant of the intermediate activation.
+enum GemmEpilogue { kEpiStore = 0, kEpiSiluQuant = 1 };
 
 struct GemmParams {
   const int32_t* eo;   // [E+1]
@@ -100,7 +104,12 @@ struct GemmParams {
   int q_stride, f_stride, nsb;
   int tile_m;
   int n_tiles;
-  int prefetch;  // K-tiles prefetched into L2 ahead of the smem loads (0: off)
+  // kEpiSiluQuant: N is the w13 output width 2*n_act; the tile's B rows are
+  // gate rows [n0, n0+128) and up rows [n_act+n0, +128)
+  int n_act;
+  int8_t* act_q;       // [sum_m, n_act] int8
+  float* act_scale;    // [scale rows, kb_act] raw block scales (in the Q buffer)
+  int kb_act;
 };
 
 struct SmemLayout {
@@ -110,14 +119,17 @@ struct SmemLayout {
   static constexpr int kStg = kB + STAGES * kTileBBytes;  // 1024-B aligned
   static constexpr int kStgWarpBytes = 32 * 64;
   static constexpr int kBar = kStg + kEpiWarps * kStgWarpBytes;  // 8-B aligned
-  static constexpr int kNumBars = 2 * STAGES + 2 * NACC + 1;
+  // full/empty ring, accumulator full/empty, final drain, and the two
+  // row-group absmax barriers of the fused SiLU-quant epilogue
+  static constexpr int kNumBars = 2 * STAGES + 2 * NACC + 1 + 2;
   static constexpr int kMisc = kBar + kNumBars * 8;   // tmem base, abort flag
-  // per-epilogue-thread slots (Q_A, Q_B per tile parity; F_A, F_B of the
-  // current tile), then the per-expert tables: m-tile prefix, scale-row
-  // offset, row count, first row
-  static constexpr int kSlots = kMisc + 16;
+  static constexpr int kRed = kMisc + 16;             // absmax slots [2 groups][3]
+  // per-epilogue-thread slots (Q_A, Q_B, Q_B(up) per tile parity; F_A, F_B,
+  // F_B(up) of the current tile), then the per-expert tables: m-tile prefix,
+  // scale-row offset, row count, first row
+  static constexpr int kSlots = kRed + 32;
   static constexpr int kSlotArray = 4 * 32 * kEpiWarps;
-  static constexpr int kPrefix = kSlots + 6 * kSlotArray;
+  static constexpr int kPrefix = kSlots + 9 * kSlotArray;
   static constexpr int bytes(int E) { return kPrefix + 4 * (E + 1) * 4 + 32; }
 };
 
@@ -191,7 +203,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const int* mt_prefix, int
   return ti;
 }
 
-template <int MODE, bool HAS_BIAS, typename OutT>
+template <int MODE, bool HAS_BIAS, typename OutT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -208,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar_accf = bar_empty + STAGES * 8;
   const uint32_t bar_acce = bar_accf + NACC * 8;
   const uint32_t bar_final = bar_acce + NACC * 8;
+  const uint32_t bar_red = bar_final + 8;  // [2]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SmemLayout::kMisc);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SmemLayout::kMisc + 4);
   int* s_tmp = reinterpret_cast<int*>(smem + SmemLayout::kA);  // scratch before the first TMA
@@ -227,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     e_row0[e] = __ldg(p.eo + e);
   }
   if (threadIdx.x == 0) *s_abort = 0;
+  if (threadIdx.x < 6) reinterpret_cast<unsigned*>(smem + SmemLayout::kRed)[threadIdx.x] = 0u;
   __syncthreads();
   block_exclusive_scan(mt_prefix, p.E, s_tmp);
   if (p.so == nullptr) block_exclusive_scan(so_prefix, p.E, s_tmp);
@@ -242,6 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_acce + 8 * a, kEpiWarps);
     }
     mbar_init(bar_final, 1);
+    // absmax groups: all 16 epilogue warps (tile_m 128) or the 8 warps of
+    // each 64-row half (tile_m 64)
+    mbar_init(bar_red, p.tile_m == 64 ? kEpiWarps / 2 : kEpiWarps);
+    mbar_init(bar_red + 8, p.tile_m == 64 ? kEpiWarps / 2 : kEpiWarps);
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -265,17 +283,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      // With p.prefetch > 0, the K-tile p.prefetch steps ahead of the one
-      // being loaded into shared memory (possibly in the next tile) is
-      // prefetched into L2 so first touches of weight tiles in HBM overlap.
-      int t = blockIdx.x;
-      TileInfo ti = decode_tile(t < total_tiles ? t : 0, mt_prefix, p.E, p.n_tiles);
-      int row0 = e_row0[ti.e] + ti.mt * BM;
-      int tn = t + gridDim.x;
-      TileInfo tin = decode_tile(tn < total_tiles ? tn : 0, mt_prefix, p.E, p.n_tiles);
-      int row0n = e_row0[tin.e] + tin.mt * BM;
-      for (; t < total_tiles && ok; t += gridDim.x) {
-        const int n0 = ti.nt * BN;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+        const int row0 = e_row0[ti.e] + ti.mt * BM;
+        const int n0 = ti.nt * (EPI == kEpiSiluQuant ? 128 : BN);
         for (int kt = 0; kt < p.kt_total; ++kt) {
           if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, s_abort, &g_err_gemm,
                          kErrProducerTimeout)) {
@@ -284,35 +295,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int kx = kt * BK - p.k_pad;
           const uint32_t fb = bar_full + 8 * stage;
+          const uint32_t b_dst = sbase + SmemLayout::kB + stage * kTileBBytes;
           mbar_arrive_expect_tx(fb, kTileABytes + kTileBBytes);
           tma_load_2d(sbase + SmemLayout::kA + stage * kTileABytes, &tmA, fb, kx, row0);
-          tma_load_3d(sbase + SmemLayout::kB + stage * kTileBBytes, &tmB, fb, kx, n0, ti.e);
-          if (p.prefetch > 0) {
-            const int pk = kt + p.prefetch;
-            if (pk < p.kt_total) {
-              const int pkx = pk * BK - p.k_pad;
-              if (pkx >= 0) {
-                tma_prefetch_l2_3d(&tmB, pkx, n0, ti.e);
-                tma_prefetch_l2_2d(&tmA, pkx, row0);
-              }
-            } else if (tn < total_tiles && pk - p.kt_total < p.kt_total) {
-              const int pkx = (pk - p.kt_total) * BK - p.k_pad;
-              if (pkx >= 0) {
-                tma_prefetch_l2_3d(&tmB, pkx, tin.nt * BN, tin.e);
-                tma_prefetch_l2_2d(&tmA, pkx, row0n);
-              }
-            }
+          if (EPI == kEpiSiluQuant) {
+            // gate rows [n0, n0+128) and the matching up rows [n_act+n0, +128)
+            tma_load_3d(b_dst, &tmB, fb, kx, n0, ti.e);
+            tma_load_3d(b_dst + kTileBBytes / 2, &tmB, fb, kx, p.n_act + n0, ti.e);
+          } else {
+            tma_load_3d(b_dst, &tmB, fb, kx, n0, ti.e);
           }
           issued[stage] = true;
           issued_phase[stage] = phase;
           if (++stage == STAGES) stage = 0, phase ^= 1;
-        }
-        ti = tin;
-        row0 = row0n;
-        tn += gridDim.x;
-        if (tn < total_tiles) {
-          tin = decode_tile(tn, mt_prefix, p.E, p.n_tiles);
-          row0n = e_row0[tin.e] + tin.mt * BM;
         }
       }
       if (!ok) {
@@ -384,33 +379,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ================= epilogue (16 warps) =================
-    // TMEM lane quadrant = warp % 4 (hardware rule), column quarter =
-    // (warp - 2) / 4: each thread owns one row and 64 columns (one 64-column
-    // weight-scale block) of the 128 x 256 tile, so a single Q_A * Q_B factor
-    // applies to all of its columns in a quant block.  Four warps share each
-    // SM sub-partition, which is what keeps the integer multiply-add pipe
-    // busy while the other warps wait for their TMEM loads.
+    // TMEM lane quadrant = warp % 4 (hardware rule), column group cq =
+    // (warp - 2) / 4.  Each thread owns one row and 64 accumulator columns:
+    //   kEpiStore:      tile columns [64cq, 64cq+64), one 64-column weight-
+    //                   scale block, so one Q_A * Q_B factor per quant block;
+    //   kEpiSiluQuant:  gate columns [32cq, +32) and the matching up columns
+    //                   [128+32cq, +32): one Q factor for each half.
+    // Four warps share each SM sub-partition, which keeps the integer
+    // multiply-add pipe busy while the other warps wait for their TMEM loads.
     const int quad = warp & 3;
     const int cq = (warp - 2) >> 2;
-    const int rl = quad * 32 + lane;  // row within the tile == TMEM lane
-    const uint32_t t_col = (static_cast<uint32_t>(quad * 32) << 16) + cq * 64;
+    const uint32_t t_lane = static_cast<uint32_t>(quad * 32) << 16;
+    constexpr bool kFused = EPI == kEpiSiluQuant;
+    auto chunk_col = [&](int c) -> uint32_t {  // TMEM column of 16-column chunk c
+      if (kFused) return (c < 2) ? 32 * cq + 16 * c : 128 + 32 * cq + 16 * (c - 2);
+      return 64 * cq + 16 * c;
+    };
+    // first output column of this thread in tile t (w13 gate column when fused)
+    auto first_col = [&](const TileInfo& u) -> int {
+      return kFused ? u.nt * 128 + 32 * cq : u.nt * BN + 64 * cq;
+    };
+    auto col_valid = [&](int col) -> bool { return col < (kFused ? p.n_act : p.N); };
     int acc = 0;
     uint32_t aphase = 0;
     bool ok = true;
     // Every lane of a warp shares one scale row (a 32-row group never
-    // straddles a tile_m boundary) and one 64-column weight block, so the
-    // factor Q_A * Q_B of a quant block is warp-uniform: lane l holds that
-    // of block (qb0 + l), and each block's factor is broadcast by shuffle.
-    // The next tile's Q factors and this tile's F factors travel by cp.async
-    // into per-thread shared-memory slots while the accumulation runs, so
-    // they take no registers from the accumulator.
-    // Slots: [Q_A, Q_B] for even local tiles, [Q_A, Q_B] for odd ones, then
-    // F_A, F_B; a slot pair is refilled only for the tile after next, so an
-    // asynchronous write never meets a pending read of the same slot.
+    // straddles a tile_m boundary) and one weight-scale block per column
+    // half, so the factor Q_A * Q_B of a quant block is warp-uniform: lane l
+    // holds that of block (qb0 + l), and each block's factor is broadcast by
+    // shuffle.  The next tile's Q factors and this tile's F factors travel by
+    // cp.async into per-thread shared-memory slots while the accumulation
+    // runs, so they take no registers from the accumulator.
+    // Slots: [Q_A, Q_B, Q_B(up)] for even local tiles, the same for odd
+    // ones, then F_A, F_B, F_B(up); a slot set is refilled only for the tile
+    // after next, so an asynchronous write never meets a pending read.
     const uint32_t s_slot = sbase + SmemLayout::kSlots + 4 * (threadIdx.x - 64);
     constexpr uint32_t kSA = SmemLayout::kSlotArray;
-    const uint32_t s_fa = s_slot + 4 * kSA;
-    const uint32_t s_fb = s_slot + 5 * kSA;
+    const uint32_t s_fa = s_slot + 6 * kSA;
+    const uint32_t s_fb = s_slot + 7 * kSA;
+    const uint32_t s_fbu = s_slot + 8 * kSA;
     auto ld_s32 = [](uint32_t a) {
       int v;
       asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
@@ -419,59 +426,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto st_s32 = [](uint32_t a, int v) {
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
     };
-    // Q_A / Q_B of quant block (qb0 + lane) of tile t, synchronously
-    auto tile_q = [&](int t, int qb0) -> int {
+    // Q_A * Q_B of quant block (qb0 + lane) of tile t, synchronously (only
+    // for more than 32 quant blocks); `up` selects the up half when fused
+    auto tile_q = [&](int t, int qb0, bool up) -> int {
       const TileInfo u = decode_tile(t, mt_prefix, p.E, p.n_tiles);
       const int wrow = u.mt * BM + quad * 32;
-      const int col = u.nt * BN + cq * 64;
+      const int col = first_col(u);
       const int qb = qb0 + lane;
-      if (MODE != kHybrid || wrow >= m_rows[u.e] || col >= p.N || qb >= p.nq) return 0;
+      if (MODE != kHybrid || wrow >= m_rows[u.e] || !col_valid(col) || qb >= p.nq) return 0;
       const int srow = so_prefix[u.e] + wrow / p.tile_m;
+      const int jb = (up ? p.n_act + col : col) / 64;
       return __ldg(p.qa + static_cast<int64_t>(srow) * p.q_stride + qb) *
-             __ldg(p.qb + (static_cast<int64_t>(u.e) * p.nsb + col / 64) * p.q_stride + qb);
+             __ldg(p.qb + (static_cast<int64_t>(u.e) * p.nsb + jb) * p.q_stride + qb);
     };
-    // Q_A / Q_B of quant blocks 0..31 (one per lane) of tile t, into the
-    // slot pair `par` asynchronously
+    // Q_A / Q_B (/ Q_B of the up half) of quant blocks 0..31 (one per lane)
+    // of tile t, into slot set `par` asynchronously
     auto fetch_q = [&](int t, int par) {
-      const uint32_t s_qa = s_slot + (2 * par) * kSA, s_qb = s_qa + kSA;
-      const int qb0 = 0;
+      const uint32_t s_qa = s_slot + (3 * par) * kSA, s_qb = s_qa + kSA, s_qbu = s_qb + kSA;
       bool any = false;
       if (MODE == kHybrid && t < total_tiles) {
         const TileInfo u = decode_tile(t, mt_prefix, p.E, p.n_tiles);
         const int wrow = u.mt * BM + quad * 32;
-        const int col = u.nt * BN + cq * 64;
-        const int qb = qb0 + lane;
-        if (wrow < m_rows[u.e] && col < p.N && qb < p.nq) {
+        const int col = first_col(u);
+        const int qb = lane;
+        if (wrow < m_rows[u.e] && col_valid(col) && qb < p.nq) {
           const int srow = so_prefix[u.e] + wrow / p.tile_m;
+          const int32_t* qb_e = p.qb + static_cast<int64_t>(u.e) * p.nsb * p.q_stride + qb;
           cp_async4(s_qa, p.qa + static_cast<int64_t>(srow) * p.q_stride + qb);
-          cp_async4(s_qb, p.qb + (static_cast<int64_t>(u.e) * p.nsb + col / 64) * p.q_stride + qb);
+          cp_async4(s_qb, qb_e + static_cast<int64_t>(col / 64) * p.q_stride);
+          if (kFused) cp_async4(s_qbu, qb_e + static_cast<int64_t>((p.n_act + col) / 64) * p.q_stride);
           any = true;
         }
       }
       if (!any) {
         st_s32(s_qa, 0);
         st_s32(s_qb, 0);
+        if (kFused) st_s32(s_qbu, 0);
       }
-    };
-    auto take_q = [&](int par) {
-      cp_async_wait_all();
-      const uint32_t s_qa = s_slot + (2 * par) * kSA;
-      return ld_s32(s_qa) * ld_s32(s_qa + kSA);
     };
     fetch_q(blockIdx.x, 0);
     int par = 0;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, par ^= 1) {
-      int qv = take_q(par);
+    int lt = 0;  // local tile counter (absmax barrier phase and slots)
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, par ^= 1, ++lt) {
+      cp_async_wait_all();
+      int qv, qvu = 0;
+      {
+        const uint32_t s_qa = s_slot + (3 * par) * kSA;
+        const int qa = ld_s32(s_qa);
+        qv = qa * ld_s32(s_qa + kSA);
+        if (kFused) qvu = qa * ld_s32(s_qa + 2 * kSA);
+      }
       fetch_q(t + gridDim.x, par ^ 1);
       {
-        // F_A, F_B of this tile (needed only by the output phase)
+        // F_A, F_B (, F_B of the up half) of this tile, for the output phase
         const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
         const int wrow0 = ti.mt * BM + quad * 32;
-        const int col0 = ti.nt * BN + cq * 64;
-        if (MODE == kHybrid && wrow0 < m_rows[ti.e] && col0 < p.N) {
+        const int col0 = first_col(ti);
+        if (MODE == kHybrid && wrow0 < m_rows[ti.e] && col_valid(col0)) {
           const int srow = so_prefix[ti.e] + wrow0 / p.tile_m;
+          const float* fb_e = p.fb + static_cast<int64_t>(ti.e) * p.nsb * p.f_stride;
           cp_async4(s_fa, p.fa + static_cast<int64_t>(srow) * p.f_stride);
-          cp_async4(s_fb, p.fb + (static_cast<int64_t>(ti.e) * p.nsb + col0 / 64) * p.f_stride);
+          cp_async4(s_fb, fb_e + static_cast<int64_t>(col0 / 64) * p.f_stride);
+          if (kFused) cp_async4(s_fbu, fb_e + static_cast<int64_t>((p.n_act + col0) / 64) * p.f_stride);
         }
       }
       int32_t W[64];
@@ -485,7 +501,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t P[16];
       for (int qb = 0; qb < p.nq && ok; ++qb) {
         const int q = __shfl_sync(0xffffffffu, qv, qb & 31);
-        if ((qb & 31) == 31 && qb + 1 < p.nq) qv = tile_q(t, qb + 1);  // K > 4096
+        const int qu = kFused ? __shfl_sync(0xffffffffu, qvu, qb & 31) : 0;
+        if ((qb & 31) == 31 && qb + 1 < p.nq) {  // K > 4096: the next 32 factors
+          qv = tile_q(t, qb + 1, false);
+          if (kFused) qvu = tile_q(t, qb + 1, true);
+        }
         if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm, kErrEpilogueTimeout)) {
           ok = false;
           break;
@@ -493,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          tmem_ld16(tmem_base + t_col + acc * BN + 16 * c, P);
+          tmem_ld16(tmem_base + t_lane + acc * BN + chunk_col(c), P);
           tmem_wait_ld(P);
           if (c == 3) {
             tc_fence_before();
@@ -502,8 +522,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (++acc == NACC) acc = 0, aphase ^= 1;
           }
           if (MODE == kHybrid) {
+            const int qc = (kFused && c >= 2) ? qu : q;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) W[16 * c + i] += q * static_cast<int32_t>(P[i]);
+            for (int i = 0; i < 16; ++i) W[16 * c + i] += qc * static_cast<int32_t>(P[i]);
           } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i) W[16 * c + i] += static_cast<int32_t>(P[i]);
@@ -511,12 +532,118 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      // ---- convert, scale, round, store ----
       const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
       const int m_e = m_rows[ti.e];
       const int wrow0 = ti.mt * BM + quad * 32;
       const int lrow = wrow0 + lane;
-      const int col0 = ti.nt * BN + cq * 64;
+      const int col0 = first_col(ti);
+      if constexpr (kFused) {
+        // ---- SiLU(gate) * up + INT8 requant of the intermediate ----
+        // mm1 = dtype(float(W) * (F_A * F_B)) (+ bias) exactly as the store
+        // epilogue would write it; then act = dtype(dtype(silu(g)) * up) and
+        // the quant of the (tile_m rows x 128 columns) block, with the same
+        // element routines as the standalone fused SiLU-quant kernel.
+        cp_async_wait_all();
+        const float fa = __int_as_float(ld_s32(s_fa));
+        const float fg = fa * __int_as_float(ld_s32(s_fb));
+        const float fu = fa * __int_as_float(ld_s32(s_fbu));
+        const bool row_ok = lrow < m_e;
+        const float* bg = HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0
+                                   : nullptr;
+        uint4 act[4];
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t g4[4], u4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = 8 * j + 2 * i;
+            if (HAS_BIAS) {
+              g4[i] = pack2<OutT>(fmaf(static_cast<float>(W[c]), fg, __ldg(bg + c)),
+                                  fmaf(static_cast<float>(W[c + 1]), fg, __ldg(bg + c + 1)));
+              u4[i] = pack2<OutT>(
+                  fmaf(static_cast<float>(W[32 + c]), fu, __ldg(bg + p.n_act + c)),
+                  fmaf(static_cast<float>(W[32 + c + 1]), fu, __ldg(bg + p.n_act + c + 1)));
+            } else {
+              g4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[c]), fg),
+                                  __fmul_rn(static_cast<float>(W[c + 1]), fg));
+              u4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[32 + c]), fu),
+                                  __fmul_rn(static_cast<float>(W[32 + c + 1]), fu));
+            }
+          }
+          uint4 a = silu_mul_chunk<OutT>(make_uint4(g4[0], g4[1], g4[2], g4[3]),
+                                         make_uint4(u4[0], u4[1], u4[2], u4[3]));
+          // rows of the next expert and columns past the intermediate size
+          // take no part in the block absmax (n_act is a multiple of 8)
+          if (!row_ok || !(col0 + 8 * j < p.n_act)) a = make_uint4(0u, 0u, 0u, 0u);
+          m = fmaxf(m, chunk_absmax<OutT>(a));
+          act[j] = a;
+        }
+        // block absmax over the tile_m rows: warp max, then a shared atomic
+        // max per row group completed by a bounded mbarrier wait (no named
+        // barrier, so a warp that gives up cannot leave the others blocked)
+        const int grp = p.tile_m == 64 ? (quad >> 1) : 0;
+        const int slot3 = lt % 3;
+        unsigned* red = reinterpret_cast<unsigned*>(smem + SmemLayout::kRed) + 3 * grp;
+        const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+        if (lane == 0) {
+          atomicMax(red + slot3, mb);
+          mbar_arrive(bar_red + 8 * grp);
+        }
+        if (!mbar_wait(bar_red + 8 * grp, static_cast<uint32_t>(lt & 1), s_abort, &g_err_gemm,
+                       kErrEpilogueTimeout)) {
+          ok = false;
+          break;
+        }
+        const float amax = __uint_as_float(*reinterpret_cast<volatile unsigned*>(red + slot3));
+        // the group's first warp clears the slot of the tile after next: every
+        // warp of the group has read it (it was this tile's previous use)
+        const bool lead = cq == 0 && quad == (p.tile_m == 64 ? 2 * grp : 0) && lane == 0;
+        if (lead) red[(lt + 2) % 3] = 0u;
+        const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 127.0f);
+        const float inv = __frcp_rn(scale);
+        const int grow0 = ti.mt * BM + (p.tile_m == 64 ? 64 * grp : 0);
+        if (lead && grow0 < m_e) {
+          const int srow = so_prefix[ti.e] + grow0 / p.tile_m;
+          p.act_scale[static_cast<int64_t>(srow) * p.kb_act + ti.nt] = scale;
+        }
+        uint32_t qw[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t w2[2];
+          if (!quant_chunk_fast<OutT>(act[j], inv, w2)) quant_chunk_exact<OutT>(act[j], inv, scale, w2);
+          qw[2 * j] = w2[0];
+          qw[2 * j + 1] = w2[1];
+        }
+        if (wrow0 + 32 <= m_e && col0 + 32 <= p.n_act) {
+          // whole warp inside the expert: 32 rows x 32 bytes staged with the
+          // 32-byte swizzle, one TMA tensor store
+          const uint32_t stg = sbase + SmemLayout::kStg + (warp - 2) * SmemLayout::kStgWarpBytes;
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t a = stg + 32 * lane + 16 * (h ^ ((lane >> 2) & 1));
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(qw[4 * h]),
+                         "r"(qw[4 * h + 1]), "r"(qw[4 * h + 2]), "r"(qw[4 * h + 3])
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, stg, col0, e_row0[ti.e] + wrow0);
+            bulk_commit();
+          }
+        } else if (row_ok) {
+          int8_t* dst = p.act_q + static_cast<int64_t>(e_row0[ti.e] + lrow) * p.n_act + col0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (col0 + 8 * j < p.n_act)
+              *reinterpret_cast<uint2*>(dst + 8 * j) = make_uint2(qw[2 * j], qw[2 * j + 1]);
+        }
+        continue;
+      }
+      // ---- convert, scale, round, store ----
       float f;
       if (MODE == kHybrid) {
         cp_async_wait_all();
@@ -653,11 +780,13 @@ int make_tmap_a(CUtensorMap* m, const int8_t* a, int64_t rows, int64_t k) {
   return I8MOE_OK;
 }
 
-int make_tmap_b(CUtensorMap* m, const int8_t* b, int64_t E, int64_t n, int64_t k) {
+// B box: all BN rows of the tile, or (fused SiLU epilogue) the 128 gate and
+// the 128 up rows as two loads
+int make_tmap_b(CUtensorMap* m, const int8_t* b, int64_t E, int64_t n, int64_t k, int box_rows) {
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(n),
                         static_cast<cuuint64_t>(E)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(n * k)};
-  cuuint32_t box[3] = {BK, BN, 1};
+  cuuint32_t box[3] = {BK, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(b), dims, strides,
                         box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -680,10 +809,23 @@ int make_tmap_out(CUtensorMap* m, void* out, int out_dtype, int64_t rows, int64_
   return I8MOE_OK;
 }
 
-template <int MODE, bool HAS_BIAS, typename OutT>
+// int8 activation output of the fused SiLU epilogue: boxes of 32 x 32 bytes
+int make_tmap_act(CUtensorMap* m, int8_t* act, int64_t rows, int64_t n_act) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(n_act), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(n_act)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, act, dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(I8MOE_ERR_CUDA, "cuTensorMapEncodeTiled(act) failed");
+  return I8MOE_OK;
+}
+
+template <int MODE, bool HAS_BIAS, typename OutT, int EPI = kEpiStore>
 int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
              const GemmParams& p, int grid, cudaStream_t st) {
-  auto kern = grouped_gemm_kernel<MODE, HAS_BIAS, OutT>;
+  auto kern = grouped_gemm_kernel<MODE, HAS_BIAS, OutT, EPI>;
   const int smem = SmemLayout::bytes(p.E) + 1024;
   static int attr_done[64] = {0};
   const int dev = current_device();
@@ -706,10 +848,23 @@ int check_device() {
   return I8MOE_OK;
 }
 
+// epi == kEpiSiluQuant: `n` is the w13 output width 2*p.n_act, `out_dtype`
+// the storage type of the intermediate (bf16/fp16), p.act_q / p.act_scale
+// the outputs.
 int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const int8_t* b,
-                GemmParams p, int64_t E, int64_t sum_m, int64_t n, int64_t k, cudaStream_t st) {
+                GemmParams p, int64_t E, int64_t sum_m, int64_t n, int64_t k, cudaStream_t st,
+                int epi = kEpiStore) {
   I8_REQUIRE(out_dtype == I8MOE_BF16 || out_dtype == I8MOE_FP16 || out_dtype == I8MOE_S32,
              "out must be bfloat16 (or float16, or int32 for the raw accumulator)");
+  if (epi == kEpiSiluQuant) {
+    I8_REQUIRE(mode == kHybrid && out_dtype != I8MOE_S32, "fused SiLU epilogue: hybrid bf16/fp16 only");
+    I8_REQUIRE(n == 2 * int64_t(p.n_act) && p.n_act % 32 == 0,
+               "fused SiLU epilogue: the intermediate size must be a multiple of 32");
+    I8_REQUIRE(p.act_q != nullptr && p.act_scale != nullptr && p.so != nullptr,
+               "fused SiLU epilogue: act_q, act_scale and scale_offsets are required");
+    I8_REQUIRE(reinterpret_cast<uintptr_t>(p.act_q) % 16 == 0, "act_q must be 16-byte aligned");
+    p.out = p.act_q;  // for the alignment check below
+  }
   I8_REQUIRE(E >= 1 && E <= kMaxExperts, "number of experts must be in [1, %d]", kMaxExperts);
   I8_REQUIRE(k % 32 == 0, "K must be divisible by 32 for INT8 tensor ops");
   I8_REQUIRE(n % 8 == 0, "N must be a multiple of 8 (16-byte output rows)");
@@ -727,10 +882,13 @@ int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const i
   CUtensorMap ta, tb;
   rc = make_tmap_a(&ta, a, sum_m, k);
   if (rc) return rc;
-  rc = make_tmap_b(&tb, b, E, n, k);
+  rc = make_tmap_b(&tb, b, E, n, k, epi == kEpiSiluQuant ? 128 : BN);
   if (rc) return rc;
   CUtensorMap to = ta;  // the raw int32 output is written without a tensor map
-  if (out_dtype != I8MOE_S32) {
+  if (epi == kEpiSiluQuant) {
+    rc = make_tmap_act(&to, p.act_q, sum_m, p.n_act);
+    if (rc) return rc;
+  } else if (out_dtype != I8MOE_S32) {
     rc = make_tmap_out(&to, p.out, out_dtype, sum_m, n);
     if (rc) return rc;
   }
@@ -740,13 +898,16 @@ int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const i
   p.K = static_cast<int>(k);
   p.kt_total = static_cast<int>((k + BK - 1) / BK);
   p.k_pad = p.kt_total * BK - p.K;
-  p.n_tiles = static_cast<int>((n + BN - 1) / BN);
+  p.n_tiles = epi == kEpiSiluQuant ? (p.n_act + 127) / 128 : static_cast<int>((n + BN - 1) / BN);
   const int64_t upper_tiles = ((sum_m + BM - 1) / BM + E) * p.n_tiles;
-  {
-    const char* pf = getenv("I8MOE_GEMM_PREFETCH");
-    p.prefetch = pf ? atoi(pf) : 0;
-  }
   const int grid = static_cast<int>(std::min<int64_t>(num_sms(current_device()), upper_tiles));
+  if (epi == kEpiSiluQuant) {
+    if (out_dtype == I8MOE_BF16)
+      return has_bias ? launch_t<kHybrid, true, __nv_bfloat16, kEpiSiluQuant>(ta, tb, to, p, grid, st)
+                      : launch_t<kHybrid, false, __nv_bfloat16, kEpiSiluQuant>(ta, tb, to, p, grid, st);
+    return has_bias ? launch_t<kHybrid, true, __half, kEpiSiluQuant>(ta, tb, to, p, grid, st)
+                    : launch_t<kHybrid, false, __half, kEpiSiluQuant>(ta, tb, to, p, grid, st);
+  }
   if (out_dtype == I8MOE_S32) {
     I8_REQUIRE(!has_bias, "the raw int32 accumulator output takes no bias");
     return mode == kHybrid ? launch_t<kHybrid, false, int32_t>(ta, tb, to, p, grid, st)
@@ -804,6 +965,54 @@ int i8moe_hybrid_grouped_gemm(const int8_t* a_q, const int32_t* a_qscale, const 
   p.tile_m = static_cast<int>(tile_m);
   return launch_gemm(kHybrid, out_dtype, bias != nullptr, a_q, b_q, p, n_expert, sum_m, n, k,
                      static_cast<cudaStream_t>(stream));
+}
+
+int i8moe_hybrid_grouped_gemm_silu_quant(
+    const int8_t* a_q, const int32_t* a_qscale, const float* a_fscale, int64_t a_scale_rows,
+    const int8_t* w13_q, const int32_t* w13_qscale, const float* w13_fscale,
+    const int32_t* expert_offsets, const int32_t* problem_sizes, const int32_t* scale_offsets,
+    const float* bias, int64_t bias_stride, int act_dtype, int64_t n_expert, int64_t sum_m,
+    int64_t n_act, int64_t k, int64_t quant_block_size, int64_t super_group_size,
+    int64_t tile_m, int64_t q_max, int8_t* act_q, int32_t* act_qscale, float* act_fscale,
+    i8moe_stream_t stream) {
+  (void)a_scale_rows;
+  I8_REQUIRE(quant_block_size > 0 && quant_block_size % BK == 0,
+             "quant_block_size must be a positive multiple of the selected TileK");
+  I8_REQUIRE(super_group_size > 0 && q_max > 0, "super_group_size and q_max must be positive");
+  I8_REQUIRE(tile_m == 64 || tile_m == 128, "tile_m must be 64 or 128");
+  I8_REQUIRE(n_act > 0, "intermediate size must be positive");
+  I8_REQUIRE(bias_stride == 0 || bias_stride == 2 * n_act, "bias must have shape [2N] or [E, 2N]");
+  I8_REQUIRE(act_qscale != nullptr && act_fscale != nullptr, "act Q/F buffers are required");
+  const int64_t nqb = (k + quant_block_size - 1) / quant_block_size;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GemmParams p{};
+  p.eo = expert_offsets;
+  p.ps = problem_sizes;
+  p.so = scale_offsets;
+  p.qa = a_qscale;
+  p.fa = a_fscale;
+  p.qb = w13_qscale;
+  p.fb = w13_fscale;
+  p.bias = bias;
+  p.bias_stride = static_cast<int>(bias_stride);
+  p.ktpq = static_cast<int>(quant_block_size / BK);
+  p.nq = static_cast<int>((((k + BK - 1) / BK) + p.ktpq - 1) / p.ktpq);
+  p.q_stride = static_cast<int>(nqb);
+  p.f_stride = static_cast<int>((nqb + super_group_size - 1) / super_group_size);
+  p.nsb = static_cast<int>((2 * n_act + 63) / 64);
+  p.tile_m = static_cast<int>(tile_m);
+  p.n_act = static_cast<int>(n_act);
+  p.act_q = act_q;
+  p.act_scale = reinterpret_cast<float*>(act_qscale);  // raw scales, factorised below
+  p.kb_act = static_cast<int>((n_act + 127) / 128);
+  int rc = launch_gemm(kHybrid, act_dtype, bias != nullptr, a_q, w13_q, p, n_expert, sum_m,
+                       2 * n_act, k, st, kEpiSiluQuant);
+  if (rc) return rc;
+  if (sum_m == 0) return I8MOE_OK;
+  const int64_t rows_upper = (sum_m + tile_m - 1) / tile_m + n_expert;
+  return launch_scales_to_qf(reinterpret_cast<const float*>(act_qscale), rows_upper,
+                             scale_offsets + n_expert, p.kb_act, q_max, super_group_size,
+                             act_qscale, act_fscale, st);
 }
 
 int i8moe_int8_grouped_mm(const int8_t* a, const int8_t* b, void* out, int out_dtype,

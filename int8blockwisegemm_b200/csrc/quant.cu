@@ -36,6 +36,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "quant_math.cuh"
 
 namespace i8moe {
 
@@ -76,34 +77,6 @@ struct TileInfo {
   int s, kb, row_start, rows;
 };
 
-__device__ __forceinline__ float max_nan(float a, float b) {
-  float r;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
-}
-__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
-__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
-
-__device__ __forceinline__ int8_t quant_exact(float x, float scale) {
-  float v = __fdiv_rn(x, scale);
-  v = fminf(fmaxf(v, -128.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(roundf(v)));
-}
-
 // Bounded spin until the producer has issued item `it`.
 __device__ __forceinline__ bool wait_issued(const int* s_issued, int it, volatile int* abort) {
   const volatile int* p = s_issued;
@@ -131,127 +104,6 @@ __device__ __forceinline__ int find_expert(const int* s_so, int E, int s) {
   return lo;
 }
 
-
-// |x|-max of one 16-byte chunk (NaN-ignoring).
-template <typename T>
-__device__ __forceinline__ float chunk_absmax(const uint4& v) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-    __nv_bfloat162 m2 = __hmax2(__habs2(h[0]), __habs2(h[1]));
-    m2 = __hmax2(m2, __hmax2(__habs2(h[2]), __habs2(h[3])));
-    return fmaxf(__low2float(m2), __high2float(m2));
-  } else if constexpr (std::is_same<T, __half>::value) {
-    const __half2* h = reinterpret_cast<const __half2*>(&v);
-    __half2 m2 = __hmax2(__habs2(h[0]), __habs2(h[1]));
-    m2 = __hmax2(m2, __hmax2(__habs2(h[2]), __habs2(h[3])));
-    return fmaxf(__low2float(m2), __high2float(m2));
-  } else {
-    const float* f = reinterpret_cast<const float*>(&v);
-    return fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
-  }
-}
-
-// Exact SiLU of one chunk (the IEEE quotient for every element).
-template <typename T>
-__device__ __noinline__ uint4 silu_mul_chunk_exact(uint4 g, uint4 u) {
-  constexpr int EPC = 16 / sizeof(T);
-  uint4 o;
-#pragma unroll
-  for (int i = 0; i < EPC; ++i) {
-    const float gf = Num<T>::to_f(reinterpret_cast<const T*>(&g)[i]);
-    const float uf = Num<T>::to_f(reinterpret_cast<const T*>(&u)[i]);
-    const float sn = Num<T>::to_f(Num<T>::from_f(__fdiv_rn(gf, 1.0f + expf(-gf))));
-    reinterpret_cast<T*>(&o)[i] = Num<T>::from_f(sn * uf);
-  }
-  return o;
-}
-
-// act = dtype(dtype(g / (1 + exp(-g))) * up) for one chunk.  The quotient is
-// g * rcp(1 + exp(-g)), within 2.5 ulp of the IEEE quotient for |g| < 80;
-// the 16-bit rounding of the two agrees unless the value lies within 4 ulp
-// of a rounding midpoint of the storage type (or, for fp16, in its subnormal
-// range) -- such chunks are recomputed with the IEEE division.
-template <typename T>
-__device__ __forceinline__ uint4 silu_mul_chunk(const uint4& g, const uint4& u) {
-  if constexpr (sizeof(T) == 4) {
-    return silu_mul_chunk_exact<T>(g, u);
-  } else {
-    constexpr int EPC = 8;
-    uint4 o;
-    bool need = false;
-#pragma unroll
-    for (int i = 0; i < EPC; ++i) {
-      const float gf = Num<T>::to_f(reinterpret_cast<const T*>(&g)[i]);
-      const float uf = Num<T>::to_f(reinterpret_cast<const T*>(&u)[i]);
-      const float y = __fdividef(gf, 1.0f + expf(-gf));
-      const uint32_t b = __float_as_uint(y);
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        need |= (((b + 4u) & 0xFFFFu) - 0x8000u) <= 8u;
-      } else {
-        need |= (((b + 4u) & 0x1FFFu) - 0x1000u) <= 8u;
-        need |= !(fabsf(y) >= 6.103515625e-05f);
-      }
-      need |= !(fabsf(gf) < 80.0f);
-      const float sn = Num<T>::to_f(Num<T>::from_f(y));
-      reinterpret_cast<T*>(&o)[i] = Num<T>::from_f(sn * uf);
-    }
-    if (need) o = silu_mul_chunk_exact<T>(g, u);
-    return o;
-  }
-}
-
-// Fast INT8 quantisation of one chunk: x * inv (packed f32x2), rounded by the
-// 1.5*2^23 trick; returns false when an element lies within 3e-5 of a
-// rounding tie (or is not finite) so the caller takes the exact path.
-template <typename T>
-__device__ __forceinline__ bool quant_chunk_fast(const uint4& v, float inv,
-                                                 uint32_t (&words)[16 / sizeof(T) / 4]) {
-  constexpr int EPC = 16 / sizeof(T);
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  const uint64_t inv2 = f2_pack(inv, inv);
-  const uint64_t magic2 = f2_pack(kMagic, kMagic);
-  const uint64_t nmagic2 = f2_pack(-kMagic, -kMagic);
-  float dmax = 0.0f;
-#pragma unroll
-  for (int w = 0; w < EPC / 4; ++w) {
-    float f[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) f[i] = Num<T>::to_f(reinterpret_cast<const T*>(&v)[4 * w + i]);
-    const uint64_t y01 = f2_mul(f2_pack(f[0], f[1]), inv2);
-    const uint64_t y23 = f2_mul(f2_pack(f[2], f[3]), inv2);
-    const uint64_t t01 = f2_add(y01, magic2);
-    const uint64_t t23 = f2_add(y23, magic2);
-    // d = y - rint(y): t - 1.5*2^23 is exact, negated by flipping the signs
-    const uint64_t d01 = f2_add(y01, f2_add(t01, nmagic2) ^ 0x8000000080000000ull);
-    const uint64_t d23 = f2_add(y23, f2_add(t23, nmagic2) ^ 0x8000000080000000ull);
-    dmax = max_nan(dmax, fabsf(f2_lo(d01)));
-    dmax = max_nan(dmax, fabsf(f2_hi(d01)));
-    dmax = max_nan(dmax, fabsf(f2_lo(d23)));
-    dmax = max_nan(dmax, fabsf(f2_hi(d23)));
-    const uint32_t lo = __byte_perm(static_cast<uint32_t>(t01), static_cast<uint32_t>(t01 >> 32), 0x0040);
-    const uint32_t hi = __byte_perm(static_cast<uint32_t>(t23), static_cast<uint32_t>(t23 >> 32), 0x0040);
-    words[w] = __byte_perm(lo, hi, 0x5410);
-  }
-  return dmax < 0.49997f;
-}
-
-// Exact reference rounding for one chunk: round_half_away(clamp(x / scale)).
-template <typename T>
-__device__ __noinline__ void quant_chunk_exact(uint4 v, float inv, float scale,
-                                               uint32_t (&words)[16 / sizeof(T) / 4]) {
-  constexpr int EPC = 16 / sizeof(T);
-  constexpr float kMagic = 12582912.0f;
-#pragma unroll
-  for (int i = 0; i < EPC; ++i) {
-    const float x = Num<T>::to_f(reinterpret_cast<const T*>(&v)[i]);
-    const float y = __fmul_rn(x, inv);
-    const float d = fabsf(y - (__fadd_rn(y, kMagic) - kMagic));
-    if (!(d < 0.49997f)) {
-      const uint32_t q = static_cast<uint8_t>(quant_exact(x, scale));
-      words[i / 4] = (words[i / 4] & ~(0xFFu << (8 * (i % 4)))) | (q << (8 * (i % 4)));
-    }
-  }
-}
 
 template <typename T, int TM, int MODE>
 struct QuantTile {
@@ -641,6 +493,22 @@ int launch_quant(int mode, const void* src, int dtype, int64_t src_rows, int64_t
 }
 
 }  // namespace
+
+// Q/F factorisation of `rows_upper` rows of raw block scales (rows past
+// *rows_dev, when given, are skipped), in place over Q.
+int launch_scales_to_qf(const float* scale, int64_t rows_upper, const int32_t* rows_dev,
+                        int64_t kb, int64_t q_max, int64_t sg, int32_t* Q, float* F,
+                        cudaStream_t st) {
+  I8_REQUIRE(rows_upper >= 0 && kb >= 0 && sg > 0 && q_max > 0, "quantize_scales: bad arguments");
+  if (rows_upper == 0 || kb == 0) return I8MOE_OK;
+  const int64_t nsg = (kb + sg - 1) / sg;
+  const int64_t warps = rows_upper * nsg;
+  scales_to_qf<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
+      scale, static_cast<int>(rows_upper), rows_dev, static_cast<int>(kb),
+      static_cast<float>(q_max), static_cast<int>(sg), static_cast<int>(nsg), Q, F);
+  return check_launch("scales_to_qf");
+}
+
 }  // namespace i8moe
 
 using namespace i8moe;

@@ -24,6 +24,7 @@ from .quant import (
     _resize_cache,
     fused_permute_quant_int8_hybrid_grouped,
     fused_silu_quant_int8_hybrid_grouped,
+    fused_w13_silu_quant_int8_hybrid_grouped,
     moe_kernel_quantize_input_int8_hybrid_grouped,
 )
 
@@ -35,6 +36,10 @@ _USE_FUSED_SILU_QUANT_W2: bool = (
     os.environ.get("VLLM_INT8_HYBRID_FUSED_SILU_QUANT", "1").strip() == "1")
 _USE_FUSED_PERMUTE_QUANT_W1: bool = (
     os.environ.get("VLLM_INT8_HYBRID_FUSED_PERMUTE_QUANT", "0").strip() == "1")
+# SiLU*up + requant inside the w13 GEMM epilogue (no reference counterpart;
+# applies when the fused SiLU quant is selected and N is a multiple of 32)
+_USE_FUSED_W13_EPILOGUE: bool = (
+    os.environ.get("INT8_HYBRID_MOE_FUSED_W13_EPILOGUE", "1").strip() == "1")
 
 
 def pick_grouped_hybrid_variant(sum_M: int, num_experts: int) -> str:
@@ -143,12 +148,25 @@ def _run_cutlass_int8_hybrid_grouped_moe(
                 a1, block_k=quant_block_size, q_max=q_max, super_group_size=super_group_size,
                 expert_offsets=expert_offsets, tile_m=tile_m))
 
-    # ---- w13 GEMM ----
-    gemm(a1q, a1_qscale, a1_fscale, w1, w1_qscale, w1_fscale, expert_offsets, problem_sizes1,
-         mm1_out, quant_block_size, super_group_size, scale_offsets=a1_scale_offsets)
+    fuse_w13 = (_USE_FUSED_W13_EPILOGUE and _USE_FUSED_SILU_QUANT_W2
+                and activation == MoEActivation.SILU and N % 32 == 0
+                and mm1_out.dtype in (torch.bfloat16, torch.float16))
+    if fuse_w13:
+        # ---- w13 GEMM with SiLU * up + requant in its epilogue ----
+        a2q, a2_qscale, a2_fscale, a2_scale_offsets = fused_w13_silu_quant_int8_hybrid_grouped(
+            a1q, a1_qscale, a1_fscale, w1, w1_qscale, w1_fscale, expert_offsets,
+            problem_sizes1, scale_offsets if scale_offsets is not None else a1_scale_offsets,
+            quant_block_size, q_max, super_group_size, tile_m, mm1_out.dtype)
+    else:
+        # ---- w13 GEMM ----
+        gemm(a1q, a1_qscale, a1_fscale, w1, w1_qscale, w1_fscale, expert_offsets,
+             problem_sizes1, mm1_out, quant_block_size, super_group_size,
+             scale_offsets=a1_scale_offsets)
 
     # ---- SiLU * up + requant ----
-    if _USE_FUSED_SILU_QUANT_W2 and activation == MoEActivation.SILU:
+    if fuse_w13:
+        pass
+    elif _USE_FUSED_SILU_QUANT_W2 and activation == MoEActivation.SILU:
         a2q, a2_qscale, a2_fscale, a2_scale_offsets = fused_silu_quant_int8_hybrid_grouped(
             mm1_out, block_k=quant_block_size, q_max=q_max, super_group_size=super_group_size,
             expert_offsets=expert_offsets, tile_m=tile_m, scale_offsets=scale_offsets)
@@ -169,7 +187,7 @@ def _run_cutlass_int8_hybrid_grouped_moe(
             eft=expert_first_token_offset, inv=inv_perm, expert_offsets=expert_offsets,
             problem_sizes1=problem_sizes1, problem_sizes2=problem_sizes2, tile_m=tile_m,
             a1q=a1q, a1_Q=a1_qscale, a1_F=a1_fscale, a1_so=a1_scale_offsets,
-            mm1=mm1_out.clone(), a2q=a2q, a2_Q=a2_qscale, a2_F=a2_fscale, a2_so=a2_scale_offsets,
+            mm1=None if fuse_w13 else mm1_out.clone(), a2q=a2q, a2_Q=a2_qscale, a2_F=a2_fscale, a2_so=a2_scale_offsets,
             mm2=mm2_out.clone())
         if _USE_FUSED_PERMUTE_QUANT_W1:
             _trace["pidx"] = permuted_idx

@@ -133,6 +133,47 @@ def fused_silu_quant_int8_hybrid_grouped(mm1_out, block_k: int, q_max: int,
     return qA, Q, F, so[:-1]
 
 
+def fused_w13_silu_quant_int8_hybrid_grouped(a_q, a_qscale, a_fscale, w1, w1_qscale, w1_fscale,
+                                             expert_offsets, problem_sizes, scale_offsets,
+                                             block_k: int, q_max: int, super_group_size: int,
+                                             tile_m: int, act_dtype, bias=None):
+    """w13 hybrid grouped GEMM with SiLU(gate)*up + INT8 requant fused into its
+    epilogue (no reference counterpart; equal to ``cutlass_int8_blockwise_
+    hybrid_grouped`` into ``act_dtype`` followed by
+    ``fused_silu_quant_int8_hybrid_grouped``, without the [M, 2N]
+    intermediate).  ``scale_offsets``: the activation scale offsets for
+    ``tile_m``, [E+1] (or [E], completed here).  Returns
+    ``(a2q, Q_A2, F_A2, scale_offsets_i32)`` like the quant functions."""
+    assert a_q.dtype == torch.int8 and w1.dtype == torch.int8
+    assert act_dtype in (torch.bfloat16, torch.float16)
+    sum_m, K = a_q.shape
+    E, two_n, K2 = w1.shape
+    assert K2 == K and two_n % 2 == 0
+    N = two_n // 2
+    eo = _eo32(expert_offsets)
+    assert eo.numel() == E + 1
+    dev = a_q.device
+    if scale_offsets is not None and scale_offsets.numel() == E + 1:
+        so = scale_offsets
+    else:
+        so = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            call("i8moe_scale_offsets", eo.data_ptr(), E, tile_m, so.data_ptr(), _stream(a_q))
+    qA, Q, F = _outputs(sum_m, N, E, tile_m, block_k, super_group_size, dev)
+    bias_stride = 0
+    if bias is not None:
+        assert bias.dtype == torch.float32 and bias.is_contiguous()
+        bias_stride = 0 if bias.ndim == 1 else bias.shape[-1]
+    with torch.cuda.device(dev):
+        call("i8moe_hybrid_grouped_gemm_silu_quant", a_q.data_ptr(), a_qscale.data_ptr(),
+             a_fscale.data_ptr(), a_qscale.shape[0], w1.data_ptr(), w1_qscale.data_ptr(),
+             w1_fscale.data_ptr(), eo.data_ptr(), problem_sizes.data_ptr(), so.data_ptr(),
+             bias.data_ptr() if bias is not None else None, bias_stride, _DT[act_dtype], E,
+             sum_m, N, K, block_k, super_group_size, tile_m, q_max, qA.data_ptr(),
+             Q.data_ptr(), F.data_ptr(), _stream(a_q))
+    return qA, Q, F, so[:-1]
+
+
 def _so(scale_offsets, E: int, device):
     """Scale-offset buffer [E+1]; ``scale_offsets`` (already computed for the
     same expert offsets and tile_m) is reused as is."""
