@@ -12,27 +12,23 @@
 // gathered hidden row hidden[permuted_idx[r] / topk] (:284-357) and
 // silu(gate) * up of the w13 output (:440-511).
 //
-// quant_kernel: a persistent grid (one CTA per SM) walks the (scale row,
-// K-block) tiles round-robin.  Warp 16 is the producer: it brings every tile
-// into a NS-deep shared-memory ring by TMA -- a dense 2-D box for contiguous
-// sources, four-row tile::gather4 boxes (row indices from permuted_idx) for
-// the permute gather -- and publishes the tile's row range next to it.  Warps
-// 0..15 form four independent consumer groups of four warps; group g takes
-// every fourth tile: pass 1 reduces the tile absmax from shared memory (warp
-// shuffles + a group named barrier), pass 2 quantises and stores the int8
-// rows, then the stage is released to the producer.  No CTA-wide barrier
-// sits on the hot path.  The block scale of every tile is written into the Q
-// buffer; scales_to_qf then factorises each (row, super-group) in place.
+// quant_rows_kernel: one CTA of 256 threads per scale row and run of four
+// K-blocks (the row range and gathered source rows are resolved once).
+// Every thread loads its 16-byte chunks of the tile straight from global
+// memory (rows gathered through permuted_idx for the permute path; gate and
+// up halves for the SiLU path) -- a warp instruction covers whole rows, so
+// the loads and the int8 stores are coalesced -- and keeps them in
+// registers: the tile absmax is reduced by warp shuffles and one CTA barrier,
+// and each thread quantises and stores its own chunks.  Four CTAs per SM keep
+// ~128 KB of loads in flight.  The block scale of every tile is written into
+// the Q buffer; scales_to_qf then factorises each (row, super-group) in place.
 //
 // x / scale is evaluated as x * (1/scale) (packed f32x2 arithmetic); a
 // product farther than 3e-5 from a rounding tie rounds exactly as the IEEE
 // quotient does (the product is within 1.6e-5 of x/scale, the IEEE quotient
 // within 3.9e-6, for |x/scale| <= 128); the rare elements closer to a tie (or
 // not finite) are recomputed with the IEEE division.
-#include <cudaTypedefs.h>
-
 #include <algorithm>
-#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -55,15 +51,17 @@ int read_quant_error(uint32_t* w, int clear) {
 
 namespace {
 
-constexpr int kGroupThreads = 128;
 constexpr int kMaxE = 2048;
+constexpr int kQuantThreads = 256;
 
 enum Mode { kDirect = 0, kGather = 1, kSilu = 2 };
 
 struct QuantArgs {
-  int M;           // rows of qA
-  int K;           // quantised columns
-  int topk;        // gather mode
+  const void* src;     // direct [M, K], gather [n_src, K], silu [M, 2K]
+  int64_t src_stride;  // elements per source row
+  int M;               // rows of qA
+  int K;               // quantised columns
+  int topk;            // gather mode
   const int32_t* pidx;
   const int32_t* eo;  // [E+1]
   const int32_t* so;  // [E+1]
@@ -73,233 +71,122 @@ struct QuantArgs {
   float* scale_out;  // [rows, Kb] block scales (the Q buffer, rewritten later)
 };
 
-struct TileInfo {
-  int s, kb, row_start, rows;
-};
-
-// Bounded spin until the producer has issued item `it`.
-__device__ __forceinline__ bool wait_issued(const int* s_issued, int it, volatile int* abort) {
-  const volatile int* p = s_issued;
-  if (*p > it) return true;
-  const uint64_t t0 = globaltimer();
-  while (*p <= it) {
-    if (*abort) return false;
-    if (globaltimer() - t0 > I8MOE_WAIT_TIMEOUT_NS) {
-      *abort = 1;
-      atomicOr(&g_err_quant, kErrEpilogueTimeout);
-      return false;
-    }
-    __nanosleep(200);
-  }
-  __threadfence_block();
-  return true;
-}
-
-__device__ __forceinline__ int find_expert(const int* s_so, int E, int s) {
-  int lo = 0, hi = E;  // last e in [0, E) with so[e] <= s
-  while (lo + 1 < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (s_so[mid] <= s) lo = mid; else hi = mid;
+// Largest e in [0, E) with so[e] <= s (so non-decreasing, so[E] > s): the
+// expert owning scale row s.  32-ary search by one warp.
+__device__ __forceinline__ int expert_of_scale_row(const int32_t* so, int E, int s, int lane) {
+  int lo = 0, hi = E;
+  while (hi - lo > 1) {
+    const int step = (hi - lo + 31) / 32;
+    const int idx = lo + lane * step;  // candidates lo, lo+step, ... below hi
+    const unsigned m = __ballot_sync(0xffffffffu, idx < hi && __ldg(so + idx) <= s);
+    const int last = 31 - __clz(m);  // lane 0 reads so[lo] <= s, so m != 0
+    lo += last * step;
+    hi = min(lo + step, hi);
   }
   return lo;
 }
 
-
 template <typename T, int TM, int MODE>
-struct QuantTile {
-  static constexpr int EPC = 16 / sizeof(T);      // elements per 16-B chunk
-  static constexpr int CPR = 128 / EPC;           // chunks per 128-wide row segment
-  static constexpr int ROWB = 128 * sizeof(T);    // bytes of one row segment
-  static constexpr int TILEB = TM * ROWB;
-  static constexpr int STAGEB = TILEB * (MODE == kSilu ? 2 : 1);
-  // ~96 KB of stages (two CTAs per SM) for the 16/32 KB tiles, the 64 KB
-  // SiLU tiles take 192 KB (one CTA per SM).
-  static constexpr int NS = STAGEB <= 16 * 1024 ? 6 : (STAGEB <= 64 * 1024 ? 3 : 1);
-  static constexpr int GROUPS = NS < 4 ? NS : 4;            // consumer groups of 4 warps
-  static constexpr int THREADS = GROUPS * kGroupThreads + 32;  // + producer warp
-  static constexpr int CHUNKS = TM * CPR;
-  static constexpr int CPT = CHUNKS / kGroupThreads;  // chunks per consumer thread
-  static_assert(CHUNKS % kGroupThreads == 0, "tile chunks");
+struct RowsTile {
+  static constexpr int EPC = 16 / sizeof(T);       // elements per 16-byte chunk
+  static constexpr int CPR = 128 / EPC;            // chunks per 128-column row segment
+  static constexpr int RPW = 32 / CPR;             // rows per warp instruction
+  static constexpr int RPP = RPW * (kQuantThreads / 32);  // rows per pass of the CTA
+  static constexpr int NP = TM / RPP;              // passes = chunks per thread
+  static constexpr int MIN_BLOCKS = (NP * (MODE == kSilu ? 2 : 1) > 8) ? 2 : 4;
+  static_assert(TM % RPP == 0, "tile rows");
 };
 
+constexpr int kKbPerCta = 4;  // K-blocks of one scale row handled by one CTA
+
 template <typename T, int TM, int MODE>
-__global__ void __launch_bounds__(QuantTile<T, TM, MODE>::THREADS, 1)
-    quant_kernel(const __grid_constant__ CUtensorMap tmap, QuantArgs a) {
-  using TL = QuantTile<T, TM, MODE>;
-  constexpr int EPC = TL::EPC, CPR = TL::CPR, NS = TL::NS, CPT = TL::CPT;
-  constexpr int kGroups = TL::GROUPS, kThreads = TL::THREADS;
-  constexpr int kConsumerThreads = kGroups * kGroupThreads;
-
-  extern __shared__ __align__(1024) uint8_t qsm_raw[];
-  uint8_t* stage_mem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(qsm_raw) + 1023) & ~uintptr_t(1023));
-  int* s_so = reinterpret_cast<int*>(stage_mem + NS * TL::STAGEB);
-  int* s_eo = s_so + (a.E + 1);
-  __shared__ __align__(8) uint64_t s_full[NS];
-  __shared__ __align__(8) uint64_t s_empty[NS];
-  __shared__ TileInfo s_info[NS];
-  __shared__ float s_red[4][2][4];
-  __shared__ int s_abort;
-  // Items handed to TMA so far.  Consumer groups take stages out of order, so
-  // a group may only wait on a stage's barrier once its own item has been
-  // issued there: then the barrier is pending exactly that item's phase and
-  // the parity wait cannot be satisfied by an older phase.
-  __shared__ int s_issued;
-
+__global__ void __launch_bounds__(kQuantThreads, (RowsTile<T, TM, MODE>::MIN_BLOCKS))
+    quant_rows_kernel(QuantArgs a) {
+  using TL = RowsTile<T, TM, MODE>;
+  constexpr int EPC = TL::EPC, CPR = TL::CPR, RPW = TL::RPW, RPP = TL::RPP, NP = TL::NP;
+  __shared__ float s_red[2][kQuantThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i <= a.E; i += kThreads) {
-    s_so[i] = __ldg(a.so + i);
-    s_eo[i] = __ldg(a.eo + i);
-  }
-  if (tid == 0) {
-    s_abort = 0;
-    s_issued = 0;
-    for (int st = 0; st < NS; ++st) {
-      mbar_init(smem_u32(&s_full[st]), 1);
-      mbar_init(smem_u32(&s_empty[st]), kGroupThreads / 32);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
-  const int total_items = s_so[a.E] * a.Kb;
-  const int n_items = blockIdx.x < total_items
-                          ? (total_items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-
-  if (warp == kConsumerThreads / 32) {
-    // ======================= producer warp =======================
-    if (lane == 0) tma_prefetch_desc(&tmap);
-    int last = -1;
-    bool ok = true;
-    // gather rows of the next item are loaded one item ahead
-    int src[4] = {0, 0, 0, 0};
-    auto item_rows = [&](int it, int& s, int& kb, int& row_start, int& row_end) {
-      const int g = blockIdx.x + it * gridDim.x;
-      s = g / a.Kb;
-      kb = g - s * a.Kb;
-      const int e = find_expert(s_so, a.E, s);
-      row_start = s_eo[e] + (s - s_so[e]) * TM;
-      row_end = min(min(s_eo[e + 1], a.M), row_start + TM);
-    };
-    auto load_src = [&](int it) {
-      int s, kb, rs, re;
-      item_rows(it, s, kb, rs, re);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = rs + 4 * lane + q;
-        src[q] = (4 * lane < TM && r < re) ? __ldg(a.pidx + r) / a.topk : 0;
-      }
-    };
-    if (MODE == kGather && n_items > 0) load_src(0);
-    for (int it = 0; it < n_items && ok; ++it) {
-      const int st = it % NS;
-      const uint32_t par = static_cast<uint32_t>(((it / NS) & 1) ^ 1);
-      if (!mbar_wait(smem_u32(&s_empty[st]), par, &s_abort, &g_err_quant, kErrProducerTimeout)) {
-        ok = false;
-        break;
-      }
-      int s, kb, row_start, row_end;
-      item_rows(it, s, kb, row_start, row_end);
-      const int col = kb * 128;
-      const uint32_t bar = smem_u32(&s_full[st]);
-      const uint32_t dst = smem_u32(stage_mem + st * TL::STAGEB);
-      if (lane == 0) s_info[st] = TileInfo{s, kb, row_start, row_end - row_start};
-      __syncwarp();
-      if (MODE == kGather) {
-        if (lane == 0) mbar_arrive_expect_tx(bar, TL::STAGEB);
-        __syncwarp();
-        if (4 * lane < TM)
-          tma_gather4(dst + lane * 4 * TL::ROWB, &tmap, bar, col, src[0], src[1], src[2], src[3]);
-        if (it + 1 < n_items) load_src(it + 1);
-      } else if (lane == 0) {
-        mbar_arrive_expect_tx(bar, TL::STAGEB);
-        tma_load_2d(dst, &tmap, bar, col, row_start);
-        if (MODE == kSilu) tma_load_2d(dst + TL::TILEB, &tmap, bar, col + a.K, row_start);
-      }
-      last = it;
-      __syncwarp();
-      if (lane == 0) {
-        __threadfence_block();
-        *reinterpret_cast<volatile int*>(&s_issued) = it + 1;
-      }
-    }
-    if (!ok && lane == 0) {
-      // never exit with TMA writes into this CTA's shared memory in flight
-      int no_abort = 0;
-      for (int it = max(0, last - NS + 1); it <= last; ++it)
-        mbar_wait(smem_u32(&s_full[it % NS]), static_cast<uint32_t>((it / NS) & 1), &no_abort,
-                  &g_err_quant, kErrDrainTimeout, 200000000ull);
-    }
+  const int groups = (a.Kb + kKbPerCta - 1) / kKbPerCta;
+  const int s = blockIdx.x / groups;
+  const int kb0 = (blockIdx.x - s * groups) * kKbPerCta;
+  if (s >= __ldg(a.so + a.E)) return;  // past the last scale row of this routing
+  // the tile rows (and, for the gather, their source rows) are shared by all
+  // K-blocks of the scale row: resolved once per CTA
+  const int e = expert_of_scale_row(a.so, a.E, s, lane);
+  const int so_e = __ldg(a.so + e);
+  const int row_start = __ldg(a.eo + e) + (s - so_e) * TM;
+  const int row_end = min(min(__ldg(a.eo + e + 1), a.M), row_start + TM);
+  const int rows = row_end - row_start;
+  if (!(so_e <= s && s < __ldg(a.so + e + 1) && row_start >= 0)) {
+    if (threadIdx.x == 0) atomicOr(&g_err_quant, kErrBadIndex);  // inconsistent offsets
     return;
   }
-
-  // ======================= consumer groups =======================
-  const int grp = warp >> 2;
-  const int gtid = tid & (kGroupThreads - 1);
-  const int gwarp = warp & 3;
-  int parity_red = 0;
-  for (int it = grp; it < n_items; it += kGroups) {
-    const int st = it % NS;
-    if (!wait_issued(&s_issued, it, &s_abort)) break;
-    if (!mbar_wait(smem_u32(&s_full[st]), static_cast<uint32_t>((it / NS) & 1), &s_abort,
-                   &g_err_quant, kErrEpilogueTimeout))
-      break;
-    const TileInfo ti = s_info[st];
-    uint8_t* tile = stage_mem + st * TL::STAGEB;
-    const int col0 = ti.kb * 128;
-
-    // ---- pass 1: (SiLU: act = dtype(silu(g)) * up, written back over g)
-    //      and the tile absmax (NaN-ignoring, as tl.max / fmaxf) ----
-    float m = 0.0f;
-#pragma unroll 1
-    for (int j = 0; j < CPT; ++j) {
-      const int c = gtid + j * kGroupThreads;
-      const int r = c / CPR, cc = c % CPR;
-      if (r < ti.rows && col0 + cc * EPC < a.K) {
-        uint4* gp = reinterpret_cast<uint4*>(tile + r * TL::ROWB + cc * 16);
-        uint4 v = *gp;
+  const int cc = lane % CPR;
+  const T* src = static_cast<const T*>(a.src);
+  int64_t src_off[NP];  // element offset of this thread's row in the source, -1 if none
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const int r = j * RPP + warp * RPW + lane / CPR;
+    src_off[j] = -1;
+    if (r < rows) {
+      int64_t srow = row_start + r;
+      if (MODE == kGather) srow = __ldg(a.pidx + srow) / a.topk;
+      src_off[j] = srow * a.src_stride;
+    }
+  }
+  const int kb1 = min(kb0 + kKbPerCta, a.Kb);
+  for (int kb = kb0; kb < kb1; ++kb) {
+    const int col = kb * 128 + cc * EPC;
+    const bool col_ok = col < a.K;
+    // ---- load this thread's chunks (all passes in flight together) ----
+    uint4 v[NP];
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      v[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (src_off[j] >= 0 && col_ok) {
+        const T* p = src + src_off[j] + col;
         if (MODE == kSilu) {
-          const uint4 u = *reinterpret_cast<const uint4*>(tile + TL::TILEB + r * TL::ROWB + cc * 16);
-          v = silu_mul_chunk<T>(v, u);
-          *gp = v;
+          const uint4 g = __ldg(reinterpret_cast<const uint4*>(p));
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + a.K));
+          v[j] = silu_mul_chunk<T>(g, u);
+        } else {
+          v[j] = __ldg(reinterpret_cast<const uint4*>(p));
         }
-        m = fmaxf(m, chunk_absmax<T>(v));
       }
     }
-    const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
-    if (lane == 0) s_red[grp][parity_red][gwarp] = __uint_as_float(mb);
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(kGroupThreads) : "memory");
-    float amax = s_red[grp][parity_red][0];
+    // ---- tile absmax (NaN-ignoring, as tl.max / fmaxf) ----
+    float m = 0.0f;
 #pragma unroll
-    for (int w = 1; w < 4; ++w) amax = fmaxf(amax, s_red[grp][parity_red][w]);
-    parity_red ^= 1;
+    for (int j = 0; j < NP; ++j) m = fmaxf(m, chunk_absmax<T>(v[j]));
+    const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+    const int buf = (kb - kb0) & 1;  // alternate, so one barrier per K-block suffices
+    if (lane == 0) s_red[buf][warp] = __uint_as_float(mb);
+    __syncthreads();
+    float amax = s_red[buf][0];
+#pragma unroll
+    for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, s_red[buf][w]);
     const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 127.0f);
     const float inv = __frcp_rn(scale);
-    if (gtid == 0) a.scale_out[static_cast<int64_t>(ti.s) * a.Kb + ti.kb] = scale;
-
-    // ---- pass 2: quantise and store ----
-#pragma unroll 1
-    for (int j = 0; j < CPT; ++j) {
-      const int c = gtid + j * kGroupThreads;
-      const int r = c / CPR, cc = c % CPR;
-      const int col = col0 + cc * EPC;
-      if (!(r < ti.rows && col < a.K)) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(tile + r * TL::ROWB + cc * 16);
+    if (tid == 0) a.scale_out[static_cast<int64_t>(s) * a.Kb + kb] = scale;
+    // ---- quantise and store ----
+    if (!col_ok) continue;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const int r = j * RPP + warp * RPW + lane / CPR;
+      if (r >= rows) continue;
       uint32_t words[EPC / 4];
-      if (!quant_chunk_fast<T>(v, inv, words)) quant_chunk_exact<T>(v, inv, scale, words);
-      if (static_cast<unsigned>(ti.row_start + r) >= static_cast<unsigned>(a.M)) {
+      if (!quant_chunk_fast<T>(v[j], inv, words)) quant_chunk_exact<T>(v[j], inv, scale, words);
+      if (static_cast<unsigned>(row_start + r) >= static_cast<unsigned>(a.M)) {
         atomicOr(&g_err_quant, kErrBadIndex);  // never store outside qA
         continue;
       }
-      int8_t* dst = a.qA + static_cast<int64_t>(ti.row_start + r) * a.K + col;
+      int8_t* dst = a.qA + static_cast<int64_t>(row_start + r) * a.K + col;
       if constexpr (EPC == 8) {
         *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[1]);
       } else {
         *reinterpret_cast<uint32_t*>(dst) = words[0];
       }
     }
-    // release the stage to the producer
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&s_empty[st]));
   }
 }
 
@@ -368,78 +255,34 @@ __global__ void __launch_bounds__(1024) scale_offsets_kernel(const int32_t* eo, 
   }
 }
 
-int dtype_size(int dtype) { return dtype == I8MOE_FP32 ? 4 : 2; }
-
-PFN_cuTensorMapEncodeTiled_v12000 g_encode_q = nullptr;
-std::once_flag g_encode_q_once;
-
-int encode_fn() {
-  std::call_once(g_encode_q_once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void* fn = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
-                                         &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      g_encode_q = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  });
-  if (!g_encode_q) return set_error(I8MOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  return I8MOE_OK;
-}
-
-// 2-D tensor map over a row-major [rows, cols] matrix with a box of
-// 128 columns x box_rows rows, no swizzle, zero fill out of bounds.
-int make_src_map(CUtensorMap* m, const void* base, int dtype, int64_t rows, int64_t cols,
-                 int box_rows) {
-  const CUtensorMapDataType dt = dtype == I8MOE_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                 : dtype == I8MOE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * dtype_size(dtype))};
-  cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = g_encode_q(m, dt, 2, const_cast<void*>(base), dims, strides, box, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(I8MOE_ERR_CUDA, "cuTensorMapEncodeTiled(quant source) failed");
-  return I8MOE_OK;
-}
-
 template <typename T, int TM, int MODE>
-int launch_quant_t(const CUtensorMap& tmap, QuantArgs a, int rows_upper, cudaStream_t st) {
-  using TL = QuantTile<T, TM, MODE>;
-  auto kern = quant_kernel<T, TM, MODE>;
-  const int smem = TL::NS * TL::STAGEB + 2 * (a.E + 1) * 4 + 1024;
-  I8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, TL::THREADS, smem) !=
-          cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
-  const int64_t items_upper = static_cast<int64_t>(rows_upper) * a.Kb;
-  const int grid = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>(static_cast<int64_t>(per_sm) * num_sms(current_device()), items_upper)));
-  kern<<<grid, TL::THREADS, smem, st>>>(tmap, a);
+int launch_quant_t(const QuantArgs& a, int rows_upper, cudaStream_t st) {
+  const int64_t items = static_cast<int64_t>(rows_upper) * ((a.Kb + kKbPerCta - 1) / kKbPerCta);
+  if (items == 0) return I8MOE_OK;
+  I8_REQUIRE(items < (int64_t(1) << 31), "quant: too many tiles");
+  quant_rows_kernel<T, TM, MODE><<<static_cast<unsigned>(items), kQuantThreads, 0, st>>>(a);
   return check_launch("quant");
 }
 
 template <int MODE>
-int launch_quant_mode(int dtype, int tm, const CUtensorMap& tmap, const QuantArgs& a,
-                      int rows_upper, cudaStream_t st) {
-  // (one CTA per SM; see quant_kernel)
+int launch_quant_mode(int dtype, int tm, const QuantArgs& a, int rows_upper, cudaStream_t st) {
   if (dtype == I8MOE_BF16) {
-    return tm == 64 ? launch_quant_t<__nv_bfloat16, 64, MODE>(tmap, a, rows_upper, st)
-                    : launch_quant_t<__nv_bfloat16, 128, MODE>(tmap, a, rows_upper, st);
+    return tm == 64 ? launch_quant_t<__nv_bfloat16, 64, MODE>(a, rows_upper, st)
+                    : launch_quant_t<__nv_bfloat16, 128, MODE>(a, rows_upper, st);
   } else if (dtype == I8MOE_FP16) {
-    return tm == 64 ? launch_quant_t<__half, 64, MODE>(tmap, a, rows_upper, st)
-                    : launch_quant_t<__half, 128, MODE>(tmap, a, rows_upper, st);
+    return tm == 64 ? launch_quant_t<__half, 64, MODE>(a, rows_upper, st)
+                    : launch_quant_t<__half, 128, MODE>(a, rows_upper, st);
   }
-  return tm == 64 ? launch_quant_t<float, 64, MODE>(tmap, a, rows_upper, st)
-                  : launch_quant_t<float, 128, MODE>(tmap, a, rows_upper, st);
+  if constexpr (MODE == kSilu) {
+    return set_error(I8MOE_ERR_INVALID, "quant: the SiLU path takes bfloat16 or float16");
+  } else {
+    return tm == 64 ? launch_quant_t<float, 64, MODE>(a, rows_upper, st)
+                    : launch_quant_t<float, 128, MODE>(a, rows_upper, st);
+  }
 }
 
-// src rows/cols describe the TMA source: direct [M, K], gather [n_src, K],
-// silu [M, 2K].
+// src: direct [M, K], gather [n_src, K] (rows picked by pidx / topk), silu
+// [M, 2K] (gate columns then up columns).
 int launch_quant(int mode, const void* src, int dtype, int64_t src_rows, int64_t src_cols,
                  int64_t M, int64_t K, const int32_t* pidx, int64_t topk, const int32_t* eo,
                  int64_t E, int64_t tm, int64_t block_k, int64_t q_max, int64_t sg, int8_t* qA,
@@ -462,12 +305,9 @@ int launch_quant(int mode, const void* src, int dtype, int64_t src_rows, int64_t
   }
   const int64_t rows_upper = (M + tm - 1) / tm + E;
   if (M == 0 || K == 0 || src_rows == 0) return I8MOE_OK;
-  int rc = encode_fn();
-  if (rc) return rc;
-  CUtensorMap tmap;
-  rc = make_src_map(&tmap, src, dtype, src_rows, src_cols, mode == kGather ? 1 : static_cast<int>(tm));
-  if (rc) return rc;
   QuantArgs a{};
+  a.src = src;
+  a.src_stride = src_cols;
   a.M = static_cast<int>(M);
   a.K = static_cast<int>(K);
   a.topk = static_cast<int>(topk);
@@ -480,9 +320,10 @@ int launch_quant(int mode, const void* src, int dtype, int64_t src_rows, int64_t
   a.scale_out = reinterpret_cast<float*>(Q);  // rewritten in place by scales_to_qf
   const int ru = static_cast<int>(std::min<int64_t>(rows_upper, INT32_MAX / std::max<int64_t>(Kb, 1)));
   const int t = static_cast<int>(tm);
-  if (mode == kDirect) rc = launch_quant_mode<kDirect>(dtype, t, tmap, a, ru, st);
-  else if (mode == kGather) rc = launch_quant_mode<kGather>(dtype, t, tmap, a, ru, st);
-  else rc = launch_quant_mode<kSilu>(dtype, t, tmap, a, ru, st);
+  int rc;
+  if (mode == kDirect) rc = launch_quant_mode<kDirect>(dtype, t, a, ru, st);
+  else if (mode == kGather) rc = launch_quant_mode<kGather>(dtype, t, a, ru, st);
+  else rc = launch_quant_mode<kSilu>(dtype, t, a, ru, st);
   if (rc) return rc;
   const int nsg = static_cast<int>((Kb + sg - 1) / sg);
   const int64_t warps = static_cast<int64_t>(ru) * nsg;
