@@ -95,6 +95,32 @@ int i8moe_moe_permute_metadata_noalloc(const int32_t* topk_ids,
                                        int32_t* inv_permuted_idx, int32_t* permuted_idx,
                                        i8moe_stream_t stream);
 
+/* No reference counterpart (the router runs before the reference's runner,
+ * which takes topk_ids / topk_weights).  Per token: the top-k experts by
+ * logits + bias (ties to the lower id) and, as their weights, the softmax of
+ * their unbiased logits (renormalised over the top-k).  logits [T, E] fp32,
+ * bias [E] fp32 or NULL, E <= 1024, topk <= min(32, E); topk_ids [T, k]
+ * int32, topk_weights [T, k] fp32. */
+int i8moe_router_topk(const float* logits, const float* bias, int64_t n_token, int64_t n_expert,
+                      int64_t topk, int32_t* topk_ids, float* topk_weights,
+                      i8moe_stream_t stream);
+
+/* No reference counterpart: i8moe_router_topk fused with the routing of
+ * i8moe_moe_route_for_gemm -- the router kernel writes topk_ids / weights and
+ * the routing histogram in one pass, then the offsets, problem sizes, scale
+ * offsets and permutation maps follow as in i8moe_moe_route_for_gemm (same
+ * arguments after topk_weights, same workspace). */
+int i8moe_router_route_for_gemm(const float* logits, const float* bias, int64_t n_token,
+                                int64_t n_expert, int64_t topk, int32_t* topk_ids,
+                                float* topk_weights, const int32_t* token_expert_indices,
+                                const int32_t* expert_map, int64_t n_local_expert,
+                                int64_t* expert_first_token_offset, int32_t* inv_permuted_idx,
+                                int32_t* permuted_idx, int32_t* expert_offsets,
+                                int32_t* problem_sizes13, int32_t* problem_sizes2,
+                                int32_t* scale_offsets, int64_t n_out1, int64_t k1,
+                                int64_t n_out2, int64_t k2, int64_t tile_m, void* workspace,
+                                size_t workspace_bytes, i8moe_stream_t stream);
+
 /* Fused-forward variant of i8moe_moe_permute_metadata (no reference
  * counterpart; it replaces the host-side torch glue of the reference runner,
  * int8_hybrid_moe/cutlass_runner.py:136-143 and the scale-offset cumsum of

@@ -29,6 +29,9 @@ PROTOTYPES = {
     "i8moe_route_workspace_size": (c_size_t, [I64, I64]),
     "i8moe_moe_permute_metadata": (I32, [P, P, P, I64, I64, I64, I64, P, P, P, P, c_size_t, P]),
     "i8moe_moe_permute_metadata_noalloc": (I32, [P, P, P, I64, I64, I64, I64, P, P, P, P]),
+    "i8moe_router_topk": (I32, [P, P, I64, I64, I64, P, P, P]),
+    "i8moe_router_route_for_gemm": (I32, [P, P, I64, I64, I64, P, P, P, P, I64, P, P, P, P, P, P,
+                                          P, I64, I64, I64, I64, I64, P, c_size_t, P]),
     "i8moe_moe_route_for_gemm": (I32, [P, P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, I64, I64,
                                        I64, I64, I64, P, c_size_t, P]),
     "i8moe_moe_permute": (I32, [P, I32, I64, P, P, P, I64, I64, I64, I64, P, P, P, P, P, c_size_t,

@@ -75,8 +75,9 @@ struct RouteArgs {
   int n_out1, k1, n_out2, k2, tile_m;
 };
 
-__device__ __forceinline__ int route_key(const RouteArgs& a, int i) {
-  int key = __ldg(a.ids + i);
+// Sort key of an expert id: the (local) expert, or key + n_expert for ids
+// mapped to no local expert, keeping the bits the reference's CUB sort uses.
+__device__ __forceinline__ int route_key_of(const RouteArgs& a, int key) {
   if (a.emap != nullptr) {
     if (key < 0 || key >= a.n_expert) {
       atomicOr(&g_err_route, kErrBadIndex);
@@ -89,6 +90,10 @@ __device__ __forceinline__ int route_key(const RouteArgs& a, int i) {
   return key & (a.nb - 1);
 }
 
+__device__ __forceinline__ int route_key(const RouteArgs& a, int i) {
+  return route_key_of(a, __ldg(a.ids + i));
+}
+
 __global__ void __launch_bounds__(kThreads) route_hist(RouteArgs a) {
   extern __shared__ int s_hist[];
   for (int b = threadIdx.x; b < a.nb; b += kThreads) s_hist[b] = 0;
@@ -98,6 +103,117 @@ __global__ void __launch_bounds__(kThreads) route_hist(RouteArgs a) {
   for (int j = 0; j < kKeysPerThread; ++j) {
     const int i = base + j * kThreads + threadIdx.x;
     if (i < a.R) atomicAdd(&s_hist[route_key(a, i)], 1);
+  }
+  __syncthreads();
+  int* out = a.hist + static_cast<int64_t>(blockIdx.x) * a.nb;
+  for (int b = threadIdx.x; b < a.nb; b += kThreads) out[b] = s_hist[b];
+}
+
+// ---------------------------------------------------------------------------
+// Router: top-k over biased logits, softmax over the selected logits
+// ---------------------------------------------------------------------------
+// One warp per token; lane l holds logits l, l+32, ...  k rounds of warp
+// arg-max pick the experts (ties to the lower expert id) by logit + bias; the
+// weights are the softmax of the selected unbiased logits (renormalised over
+// the top-k), as the benchmark's seeded router builds them.  With
+// `a.hist != nullptr` the CTA also writes the routing histogram of its key
+// chunk (the route_hist output), so routing can start from the logits.
+struct RouterArgs {
+  const float* logits;  // [T, E]
+  const float* bias;    // [E] or null
+  int T, E, k;
+  int32_t* ids;         // [T, k]
+  float* weights;       // [T, k]
+};
+
+// Returns the expert picked in round `lane` (lanes 0..k-1).
+template <int VPL>
+__device__ __forceinline__ int router_token(const RouterArgs& r, int t, int lane) {
+  const float* row = r.logits + static_cast<int64_t>(t) * r.E;
+  float v[VPL], sv[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < r.E ? __ldg(row + e) : 0.f;
+    sv[i] = e < r.E ? v[i] + (r.bias ? __ldg(r.bias + e) : 0.f) : -INFINITY;
+  }
+  unsigned taken = 0u;
+  int my_id = 0;
+  float my_logit = -INFINITY;
+  for (int j = 0; j < r.k; ++j) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int e = lane + 32 * i;
+      if (!(taken >> i & 1u) && e < r.E && (sv[i] > bv || be == 0x7fffffff)) {
+        bv = sv[i];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    // the owner marks it and broadcasts the unbiased logit
+    float lg = 0.f;
+    if ((be & 31) == lane) {
+      const int i = be >> 5;
+#pragma unroll
+      for (int q = 0; q < VPL; ++q)
+        if (q == i) {
+          taken |= 1u << q;
+          lg = v[q];
+        }
+    }
+    lg = __shfl_sync(0xffffffffu, lg, be & 31);
+    if (lane == j) {
+      my_id = be;
+      my_logit = lg;
+    }
+  }
+  // softmax over the k selected logits (lanes 0..k-1)
+  float m = lane < r.k ? my_logit : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float ex = lane < r.k ? expf(my_logit - m) : 0.f;
+  float sum = ex;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane < r.k) {
+    r.ids[static_cast<int64_t>(t) * r.k + lane] = my_id;
+    r.weights[static_cast<int64_t>(t) * r.k + lane] = __fdiv_rn(ex, sum);
+  }
+  return my_id;
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs r, RouteArgs a) {
+  extern __shared__ int s_hist[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (a.hist == nullptr) {
+    const int t = blockIdx.x * (kThreads / 32) + warp;
+    if (t < r.T) router_token<VPL>(r, t, lane);
+    return;
+  }
+  // fused with route_hist: this CTA owns keys [c*kChunk, (c+1)*kChunk)
+  for (int b = threadIdx.x; b < a.nb; b += kThreads) s_hist[b] = 0;
+  __syncthreads();
+  const int key0 = blockIdx.x * kChunk;
+  const int key1 = min(key0 + kChunk, a.R);
+  const int t0 = key0 / r.k, t1 = (key1 + r.k - 1) / r.k;
+  for (int t = t0 + warp; t < t1; t += kThreads / 32) {
+    // a token straddling two chunks is routed by both CTAs, identically
+    const int id = router_token<VPL>(r, t, lane);
+    if (lane < r.k) {
+      const int i = t * r.k + lane;
+      if (i >= key0 && i < key1) atomicAdd(&s_hist[route_key_of(a, id)], 1);
+    }
   }
   __syncthreads();
   int* out = a.hist + static_cast<int64_t>(blockIdx.x) * a.nb;
@@ -369,10 +485,14 @@ struct FusedExtras {
   int n_out1 = 0, k1 = 0, n_out2 = 0, k2 = 0, tile_m = 128;
 };
 
+int router_vpl(int64_t E) { return E <= 256 ? 8 : (E <= 512 ? 16 : (E <= 1024 ? 32 : 0)); }
+
+// r != nullptr: the first routing kernel is the router (top-k + softmax from
+// logits), which writes topk_ids/weights and the chunk histogram.
 int launch_route(const int32_t* topk_ids, const int32_t* tei, const int32_t* emap,
                  int64_t n_token, int64_t topk, int64_t n_expert, int64_t n_local, int64_t* eft,
                  int32_t* inv, int32_t* pidx, void* ws, size_t ws_bytes, cudaStream_t st,
-                 const FusedExtras& fx) {
+                 const FusedExtras& fx, const RouterArgs* router = nullptr) {
   I8_REQUIRE(n_token >= 0 && topk > 0, "moe_permute: bad n_token/topk");
   I8_REQUIRE(n_expert >= 1 && n_expert <= 2048, "moe_permute: n_expert must be in [1, 2048]");
   I8_REQUIRE(n_local >= 0 && n_local <= n_expert,
@@ -412,7 +532,14 @@ int launch_route(const int32_t* topk_ids, const int32_t* tei, const int32_t* ema
     I8_CUDA(cudaFuncSetAttribute(route_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem_scatter)));
   }
-  route_hist<<<chunks, kThreads, smem_hist, st>>>(a);
+  if (router != nullptr) {
+    const int vpl = router_vpl(router->E);
+    if (vpl == 8) router_kernel<8><<<chunks, kThreads, smem_hist, st>>>(*router, a);
+    else if (vpl == 16) router_kernel<16><<<chunks, kThreads, smem_hist, st>>>(*router, a);
+    else router_kernel<32><<<chunks, kThreads, smem_hist, st>>>(*router, a);
+  } else {
+    route_hist<<<chunks, kThreads, smem_hist, st>>>(a);
+  }
   route_scan<<<1, 1024, 0, st>>>(a);
   route_scatter<<<chunks, kThreads, smem_scatter, st>>>(a, emap != nullptr ? 1 : 0);
   return check_launch("route kernels");
@@ -540,6 +667,57 @@ int i8moe_moe_permute_metadata_noalloc(const int32_t* topk_ids,
   return launch_route_noalloc(topk_ids, token_expert_indices, expert_map, n_token, topk, n_expert,
                               n_local_expert, expert_first_token_offset, inv_permuted_idx,
                               permuted_idx, static_cast<cudaStream_t>(stream));
+}
+
+int i8moe_router_topk(const float* logits, const float* bias, int64_t n_token, int64_t n_expert,
+                      int64_t topk, int32_t* topk_ids, float* topk_weights,
+                      i8moe_stream_t stream) {
+  I8_REQUIRE(n_token >= 0 && n_token < (int64_t(1) << 31), "router: bad n_token");
+  I8_REQUIRE(router_vpl(n_expert) > 0, "router: n_expert must be in [1, 1024]");
+  I8_REQUIRE(topk >= 1 && topk <= 32 && topk <= n_expert, "router: topk must be in [1, min(32, E)]");
+  if (n_token == 0) return I8MOE_OK;
+  RouterArgs r{logits, bias, static_cast<int>(n_token), static_cast<int>(n_expert),
+               static_cast<int>(topk), topk_ids, topk_weights};
+  RouteArgs a{};  // a.hist == nullptr: router only
+  const unsigned grid = static_cast<unsigned>((n_token + kThreads / 32 - 1) / (kThreads / 32));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vpl = router_vpl(n_expert);
+  if (vpl == 8) router_kernel<8><<<grid, kThreads, 0, st>>>(r, a);
+  else if (vpl == 16) router_kernel<16><<<grid, kThreads, 0, st>>>(r, a);
+  else router_kernel<32><<<grid, kThreads, 0, st>>>(r, a);
+  return check_launch("router");
+}
+
+int i8moe_router_route_for_gemm(const float* logits, const float* bias, int64_t n_token,
+                                int64_t n_expert, int64_t topk, int32_t* topk_ids,
+                                float* topk_weights, const int32_t* token_expert_indices,
+                                const int32_t* expert_map, int64_t n_local_expert,
+                                int64_t* expert_first_token_offset, int32_t* inv_permuted_idx,
+                                int32_t* permuted_idx, int32_t* expert_offsets,
+                                int32_t* problem_sizes13, int32_t* problem_sizes2,
+                                int32_t* scale_offsets, int64_t n_out1, int64_t k1,
+                                int64_t n_out2, int64_t k2, int64_t tile_m, void* workspace,
+                                size_t workspace_bytes, i8moe_stream_t stream) {
+  I8_REQUIRE(router_vpl(n_expert) > 0, "router: n_expert must be in [1, 1024]");
+  I8_REQUIRE(topk >= 1 && topk <= 32 && topk <= n_expert, "router: topk must be in [1, min(32, E)]");
+  I8_REQUIRE(tile_m > 0, "route_for_gemm: tile_m must be positive");
+  I8_REQUIRE(expert_offsets && problem_sizes13 && problem_sizes2 && scale_offsets,
+             "route_for_gemm: every output must be given");
+  RouterArgs r{logits, bias, static_cast<int>(n_token), static_cast<int>(n_expert),
+               static_cast<int>(topk), topk_ids, topk_weights};
+  FusedExtras fx;
+  fx.eo32 = expert_offsets;
+  fx.ps1 = problem_sizes13;
+  fx.ps2 = problem_sizes2;
+  fx.so = scale_offsets;
+  fx.n_out1 = static_cast<int>(n_out1);
+  fx.k1 = static_cast<int>(k1);
+  fx.n_out2 = static_cast<int>(n_out2);
+  fx.k2 = static_cast<int>(k2);
+  fx.tile_m = static_cast<int>(tile_m);
+  return launch_route(topk_ids, token_expert_indices, expert_map, n_token, topk, n_expert,
+                      n_local_expert, expert_first_token_offset, inv_permuted_idx, permuted_idx,
+                      workspace, workspace_bytes, static_cast<cudaStream_t>(stream), fx, &r);
 }
 
 int i8moe_moe_route_for_gemm(const int32_t* topk_ids, const int32_t* token_expert_indices,

@@ -71,6 +71,56 @@ def moe_route_for_gemm(topk_ids, n_token: int, n_expert: int, n_local_expert: in
     return eft, inv.flatten(), pidx, eo, ps1, ps2, so
 
 
+def router_topk(logits, topk: int, bias=None):
+    """Extension (the router upstream of the runner): top-k experts of each
+    token by logits + bias, weights = softmax of their unbiased logits.
+    Returns (topk_weights fp32 [T, k], topk_ids int32 [T, k])."""
+    from ._lib import call
+    assert logits.dtype == torch.float32 and logits.is_contiguous() and logits.is_cuda
+    T, E = logits.shape
+    ids = torch.empty(T, topk, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, topk, dtype=torch.float32, device=logits.device)
+    if bias is not None:
+        assert bias.dtype == torch.float32 and bias.numel() == E and bias.is_contiguous()
+    with torch.cuda.device(logits.device):
+        call("i8moe_router_topk", logits.data_ptr(),
+             bias.data_ptr() if bias is not None else None, T, E, topk, ids.data_ptr(),
+             w.data_ptr(), torch.cuda.current_stream(logits.device).cuda_stream)
+    return w, ids
+
+
+def router_route_for_gemm(logits, topk: int, n_local_expert: int, expert_map, n_out1: int,
+                          k1: int, n_out2: int, k2: int, tile_m: int, bias=None):
+    """Extension: ``router_topk`` and ``moe_route_for_gemm`` in one pass (the
+    router kernel also builds the routing histogram).  Returns
+    (topk_weights, topk_ids, expert_first_token_offset, inv_permuted_idx
+    (flat), permuted_idx, expert_offsets_i32, problem_sizes13,
+    problem_sizes2, scale_offsets_i32)."""
+    from ._lib import call
+    assert logits.dtype == torch.float32 and logits.is_contiguous() and logits.is_cuda
+    T, E = logits.shape
+    dev = logits.device
+    ids = torch.empty(T, topk, dtype=torch.int32, device=dev)
+    w = torch.empty(T, topk, dtype=torch.float32, device=dev)
+    tei, eft, pidx, inv = _alloc(T, topk, n_local_expert, dev)
+    eo = torch.empty(n_local_expert + 1, dtype=torch.int32, device=dev)
+    ps1 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)
+    ps2 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)
+    so = torch.empty(n_local_expert + 1, dtype=torch.int32, device=dev)
+    from ._lib import LIB
+    ws = torch.empty(max(1, LIB.i8moe_route_workspace_size(T * topk, E)), dtype=torch.uint8,
+                     device=dev)
+    emap = expert_map.to(torch.int32).contiguous() if expert_map is not None else None
+    with torch.cuda.device(dev):
+        call("i8moe_router_route_for_gemm", logits.data_ptr(),
+             bias.data_ptr() if bias is not None else None, T, E, topk, ids.data_ptr(),
+             w.data_ptr(), tei.data_ptr(), emap.data_ptr() if emap is not None else None,
+             n_local_expert, eft.data_ptr(), inv.data_ptr(), pidx.data_ptr(), eo.data_ptr(),
+             ps1.data_ptr(), ps2.data_ptr(), so.data_ptr(), n_out1, k1, n_out2, k2, tile_m,
+             ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+    return w, ids, eft, inv.flatten(), pidx, eo, ps1, ps2, so
+
+
 def moe_unpermute(out, permuted_hidden_states, topk_weights, inv_permuted_idx,
                   expert_first_token_offset=None) -> None:
     """Top-k weighted reduction back to token order."""

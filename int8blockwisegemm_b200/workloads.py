@@ -128,4 +128,4 @@ def make_inputs(cfg: MoEConfig, seed: int | None = None) -> dict:
     f2 = torch.empty(E, math.ceil(K / 64), math.ceil(kb2 / cfg.sg)).log_normal_(
         cfg.f_mu, 0.5, generator=g)
     return dict(hidden=hidden, topk_ids=topk_ids, topk_weights=topk_weights, w13=w13, w2=w2,
-                w13_q=q13, w13_f=f13, w2_q=q2, w2_f=f2)
+                w13_q=q13, w13_f=f13, w2_q=q2, w2_f=f2, router_logits=logits, router_bias=bias)

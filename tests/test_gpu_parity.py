@@ -502,3 +502,40 @@ def test_fused_w13_epilogue_matches_gemm_then_silu_quant(m, cname):
     assert torch.equal(ta["mm2"][:v].view(bits[out_a.dtype]), tb["mm2"][:v].view(bits[out_a.dtype]))
     assert torch.equal(out_a.view(bits[out_a.dtype]), out_b.view(bits[out_a.dtype]))
     assert m._lib.device_error(0) == 0
+
+
+# ---------------------------------------------------------------------------
+# router (extension upstream of the runner)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("cname", ["default", "skewed", "large", "mid"])
+def test_router_topk_matches_seeded_router(m, cname):
+    """Top-k by logits + bias and the softmax of the selected logits, against
+    the CPU recipe that produced the workload's topk_ids / topk_weights."""
+    cfg, inp = inputs(cname)
+    logits = inp["router_logits"].to(DEV)
+    bias = inp["router_bias"].float().to(DEV)
+    w, ids = m.permute.router_topk(logits, cfg.topk, bias)
+    torch.cuda.synchronize()
+    assert torch.equal(ids.cpu(), inp["topk_ids"])
+    # torch's CPU softmax evaluates exp and the sum in its own vector order:
+    # a few fp32 ulp apart (relative ~1e-6)
+    ud = ulp_diff(npf(w), inp["topk_weights"].numpy(), "fp32")
+    assert ud.max() <= 8, ud.max()
+
+
+@pytest.mark.parametrize("cname", ["default", "mid", "tiny"])
+def test_router_fused_routing_matches_separate_calls(m, cname):
+    cfg, inp = inputs(cname)
+    logits = inp["router_logits"].to(DEV)
+    bias = inp["router_bias"].float().to(DEV)
+    T, k, E, N, K = cfg.T, cfg.topk, cfg.E, cfg.N, cfg.K
+    tm = 128 if T * k / E > 70 else 64
+    fused = m.permute.router_route_for_gemm(logits, k, E, None, 2 * N, K, K, N, tm, bias)
+    w, ids = m.permute.router_topk(logits, k, bias)
+    sep = m.permute.moe_route_for_gemm(ids, T, E, E, None, 2 * N, K, K, N, tm)
+    torch.cuda.synchronize()
+    assert torch.equal(fused[0], w) and torch.equal(fused[1], ids)
+    for a, b in zip(fused[2:], sep):
+        assert torch.equal(a, b)
+    assert m._lib.device_error(0) == 0
