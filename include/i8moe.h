@@ -211,6 +211,18 @@ int i8moe_quant_silu(const void* mm1, int dtype, int64_t M, int64_t N,
                      int32_t* Q, float* F, int32_t* scale_offsets, int scale_offsets_ready,
                      i8moe_stream_t stream);
 
+/* Replaces the reference's weight preparation _quantize_blockwise_int8
+ * (bench_int8_hybrid_moe.py:98-120, called with block_n = 64, block_k =
+ * quant_block_size at :220-229), which is host-side torch code there.  Per
+ * (expert, 64-row, 128-column) block of w [E, N, K] (bf16 / fp16 / fp32):
+ * scale = max(absmax, 1e-10) / 127 and q = clamp(rint(w / scale), -128, 127)
+ * (ties to even), ragged blocks padded with zeros.  q [E, N, K] int8, scale
+ * [E, ceil(N/64), ceil(K/128)] fp32.  The GEMM's Q_B / F_B follow with
+ * i8moe_quantize_scales over the [E * ceil(N/64), ceil(K/128)] view. */
+int i8moe_quantize_weights(const void* w, int dtype, int64_t n_expert, int64_t n, int64_t k,
+                           int64_t block_n, int64_t block_k, int8_t* q, float* scale,
+                           i8moe_stream_t stream);
+
 /* Replaces quantize_scales_for_hybrid (int8_hybrid_moe/quant.py:52-140) on a
  * standalone fp32 scale matrix [rows, kb]. */
 int i8moe_quantize_scales(const float* scale, int64_t rows, int64_t kb, int64_t q_max,

@@ -44,6 +44,7 @@ PROTOTYPES = {
     "i8moe_quant_permute": (I32, [P, I32, I64, I64, P, I64, I64, P, I64, I64, I64, I64, I64, P, P,
                                   P, P, I32, P]),
     "i8moe_quant_silu": (I32, [P, I32, I64, I64, P, I64, I64, I64, I64, I64, P, P, P, P, I32, P]),
+    "i8moe_quantize_weights": (I32, [P, I32, I64, I64, I64, I64, I64, P, P, P]),
     "i8moe_quantize_scales": (I32, [P, I64, I64, I64, I64, P, P, P]),
     "i8moe_hybrid_grouped_gemm": (I32, [P, P, P, I64, P, P, P, P, P, P, P, I64, P, I32, I64, I64,
                                         I64, I64, I64, I64, I64, P]),

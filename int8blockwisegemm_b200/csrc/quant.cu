@@ -190,6 +190,66 @@ __global__ void __launch_bounds__(kQuantThreads, (RowsTile<T, TM, MODE>::MIN_BLO
   }
 }
 
+// ---------------------------------------------------------------------------
+// Weight preparation (reference bench_int8_hybrid_moe.py:98-120): blockwise
+// INT8 weights, one CTA per (expert, 64-row, 128-column) block.  Rows and
+// columns past the tensor are the reference's zero padding: they join the
+// absmax as zeros and are not stored.
+// ---------------------------------------------------------------------------
+constexpr int kWBlockN = 64, kWBlockK = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) weight_quant_kernel(const T* __restrict__ w,
+                                                                     int N, int K, int nb, int kb,
+                                                                     int8_t* __restrict__ q,
+                                                                     float* __restrict__ scale) {
+  constexpr int EPC = 16 / sizeof(T);
+  constexpr int CPR = kWBlockK / EPC;              // chunks per row of the block
+  constexpr int RPP = kQuantThreads / CPR;         // rows per pass
+  constexpr int NP = kWBlockN / RPP;               // chunks per thread
+  __shared__ float s_red[kQuantThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int blk = blockIdx.x;
+  const int bk = blk % kb, bn = (blk / kb) % nb, e = blk / (kb * nb);
+  const int col = bk * kWBlockK + (tid % CPR) * EPC;
+  const int64_t base = static_cast<int64_t>(e) * N * K;
+  uint4 v[NP];
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const int row = bn * kWBlockN + j * RPP + tid / CPR;
+    v[j] = make_uint4(0u, 0u, 0u, 0u);
+    if (row < N && col < K)
+      v[j] = __ldg(reinterpret_cast<const uint4*>(w + base + static_cast<int64_t>(row) * K + col));
+  }
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NP; ++j) m = fmaxf(m, chunk_absmax<T>(v[j]));
+  const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+  if (lane == 0) s_red[warp] = __uint_as_float(mb);
+  __syncthreads();
+  float amax = s_red[0];
+#pragma unroll
+  for (int i = 1; i < kQuantThreads / 32; ++i) amax = fmaxf(amax, s_red[i]);
+  const float sc = __fdiv_rn(fmaxf(amax, 1e-10f), 127.0f);
+  const float inv = __frcp_rn(sc);
+  if (tid == 0) scale[blk] = sc;
+  if (col >= K) return;
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const int row = bn * kWBlockN + j * RPP + tid / CPR;
+    if (row >= N) continue;
+    uint32_t words[EPC / 4];
+    // the fast rounding equals rint wherever it does not defer (no ties)
+    if (!quant_chunk_fast<T>(v[j], inv, words)) quant_chunk_exact_rne<T>(v[j], sc, words);
+    int8_t* dst = q + base + static_cast<int64_t>(row) * K + col;
+    if constexpr (EPC == 8) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[1]);
+    } else {
+      *reinterpret_cast<uint32_t*>(dst) = words[0];
+    }
+  }
+}
+
 // Q/F factorisation of fp32 block scales, one warp per (row, super-group).
 // `scale` and `Q` may alias (in-place): every lane rewrites only the entries
 // it read, after the group maximum has been reduced.  When `rows_dev` is
@@ -394,6 +454,37 @@ int i8moe_quant_silu(const void* mm1, int dtype, int64_t M, int64_t N,
   return launch_quant(kSilu, mm1, dtype, M, 2 * N, M, N, nullptr, 1, expert_offsets, n_expert,
                       tile_m, block_k, q_max, super_group_size, qA, Q, F, scale_offsets,
                       scale_offsets_ready, static_cast<cudaStream_t>(stream));
+}
+
+int i8moe_quantize_weights(const void* w, int dtype, int64_t n_expert, int64_t n, int64_t k,
+                           int64_t block_n, int64_t block_k, int8_t* q, float* scale,
+                           i8moe_stream_t stream) {
+  I8_REQUIRE(dtype == I8MOE_BF16 || dtype == I8MOE_FP16 || dtype == I8MOE_FP32,
+             "quantize_weights: w must be float32, float16 or bfloat16");
+  I8_REQUIRE(block_n == kWBlockN && block_k == kWBlockK,
+             "quantize_weights: blocks of 64 x 128 (the GEMM's weight-scale blocks) only");
+  I8_REQUIRE(n_expert >= 0 && n > 0 && k > 0, "quantize_weights: bad shape");
+  I8_REQUIRE(k % (dtype == I8MOE_FP32 ? 4 : 8) == 0, "quantize_weights: K must allow 16-byte rows");
+  I8_REQUIRE((reinterpret_cast<uintptr_t>(w) % 16 == 0) && (reinterpret_cast<uintptr_t>(q) % 8 == 0),
+             "quantize_weights: w must be 16-byte and q 8-byte aligned");
+  const int64_t nb = (n + kWBlockN - 1) / kWBlockN, kb = (k + kWBlockK - 1) / kWBlockK;
+  const int64_t blocks = n_expert * nb * kb;
+  I8_REQUIRE(blocks < (int64_t(1) << 31) && n_expert * n * k < (int64_t(1) << 62),
+             "quantize_weights: tensor too large");
+  if (blocks == 0) return I8MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned g = static_cast<unsigned>(blocks);
+  const int N = static_cast<int>(n), K = static_cast<int>(k);
+  if (dtype == I8MOE_BF16)
+    weight_quant_kernel<__nv_bfloat16><<<g, kQuantThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(w), N, K, static_cast<int>(nb), static_cast<int>(kb), q, scale);
+  else if (dtype == I8MOE_FP16)
+    weight_quant_kernel<__half><<<g, kQuantThreads, 0, st>>>(
+        static_cast<const __half*>(w), N, K, static_cast<int>(nb), static_cast<int>(kb), q, scale);
+  else
+    weight_quant_kernel<float><<<g, kQuantThreads, 0, st>>>(
+        static_cast<const float*>(w), N, K, static_cast<int>(nb), static_cast<int>(kb), q, scale);
+  return check_launch("quantize_weights");
 }
 
 int i8moe_quantize_scales(const float* scale, int64_t rows, int64_t kb, int64_t q_max,

@@ -173,5 +173,20 @@ __device__ __noinline__ void quant_chunk_exact(uint4 v, float inv, float scale,
   }
 }
 
+// As quant_chunk_exact, with ties rounded to even (torch.round / rint), for the
+// weight preparation: clamp(rint(x / scale)).
+template <typename T>
+__device__ __noinline__ void quant_chunk_exact_rne(uint4 v, float scale,
+                                                   uint32_t (&words)[16 / sizeof(T) / 4]) {
+  constexpr int EPC = 16 / sizeof(T);
+#pragma unroll
+  for (int i = 0; i < EPC; ++i) {
+    const float x = Num<T>::to_f(reinterpret_cast<const T*>(&v)[i]);
+    const float q = fminf(fmaxf(rintf(__fdiv_rn(x, scale)), -128.0f), 127.0f);
+    const uint32_t b = static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(q)));
+    words[i / 4] = (words[i / 4] & ~(0xFFu << (8 * (i % 4)))) | (b << (8 * (i % 4)));
+  }
+}
+
 }  // namespace
 }  // namespace i8moe

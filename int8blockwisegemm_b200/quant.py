@@ -133,6 +133,34 @@ def fused_silu_quant_int8_hybrid_grouped(mm1_out, block_k: int, q_max: int,
     return qA, Q, F, so[:-1]
 
 
+def quantize_weights_blockwise_int8(w: torch.Tensor, block_n: int = 64, block_k: int = 128):
+    """Blockwise INT8 weights on the device, the reference's weight
+    preparation ``_quantize_blockwise_int8`` (bench_int8_hybrid_moe.py:98-120).
+    Returns (q int8 [E, N, K], scale fp32 [E, ceil(N/64), ceil(K/128)])."""
+    assert w.ndim == 3 and w.is_cuda and w.dtype in _DT
+    w = w.contiguous()
+    E, N, K = w.shape
+    q = torch.empty((E, N, K), dtype=torch.int8, device=w.device)
+    scale = torch.empty((E, cdiv(N, block_n), cdiv(K, block_k)), dtype=torch.float32,
+                        device=w.device)
+    with torch.cuda.device(w.device):
+        call("i8moe_quantize_weights", w.data_ptr(), _DT[w.dtype], E, N, K, block_n, block_k,
+             q.data_ptr(), scale.data_ptr(), _stream(w))
+    return q, scale
+
+
+def prepare_hybrid_weights(w: torch.Tensor, q_max: int, super_group_size: int,
+                           block_n: int = 64, block_k: int = 128):
+    """Device version of the reference's weight preparation: blockwise INT8
+    weights plus the hybrid (Q, F) factorisation of their scales along K
+    (bench_int8_hybrid_moe.py:228-244).  Returns (q [E, N, K] int8,
+    Q [E, N/64, Kb] int32, F [E, N/64, num_super_groups] fp32)."""
+    q, scale = quantize_weights_blockwise_int8(w, block_n, block_k)
+    E, Nb, Kb = scale.shape
+    Q, F = quantize_scales_for_hybrid(scale.reshape(E * Nb, Kb), q_max, super_group_size)
+    return q, Q.reshape(E, Nb, Kb), F.reshape(E, Nb, -1)
+
+
 def fused_w13_silu_quant_int8_hybrid_grouped(a_q, a_qscale, a_fscale, w1, w1_qscale, w1_fscale,
                                              expert_offsets, problem_sizes, scale_offsets,
                                              block_k: int, q_max: int, super_group_size: int,

@@ -328,6 +328,26 @@ def fused_silu_quant(mm1_out, expert_offsets, tile_m: int, dtype: str, block_k: 
     return _quant_generic(get_x, M, N, expert_offsets, tile_m, block_k)
 
 
+def quantize_weights_blockwise(w, block_n: int = 64, block_k: int = 128):
+    """Blockwise INT8 weights, bench_int8_hybrid_moe.py:98-120: per (expert,
+    block_n rows, block_k columns) block, scale = max(absmax, 1e-10) / 127 and
+    q = clamp(rint(w / scale), -128, 127) (torch.round: ties to even); the
+    zero padding of ragged blocks takes part in the absmax.
+
+    Returns (q int8 [E, N, K], scale f32 [E, ceil(N/block_n), ceil(K/block_k)])."""
+    w = np.asarray(w, np.float32)
+    E, N, K = w.shape
+    nb, kb = -(-N // block_n), -(-K // block_k)
+    pad = np.zeros((E, nb * block_n, kb * block_k), np.float32)
+    pad[:, :N, :K] = w
+    view = pad.reshape(E, nb, block_n, kb, block_k).transpose(0, 1, 3, 2, 4)
+    amax = np.abs(view).max(axis=(-1, -2))
+    scale = (np.maximum(amax, np.float32(1e-10)) / np.float32(127.0)).astype(np.float32)
+    qv = np.clip(np.rint(view / scale[..., None, None]), -128, 127).astype(np.int8)
+    q = qv.transpose(0, 1, 3, 2, 4).reshape(E, nb * block_n, kb * block_k)[:, :N, :K]
+    return np.ascontiguousarray(q), scale
+
+
 def quantize_scales_for_hybrid(scale, q_max: int = 64, super_group_size: int | None = None):
     """Two-level (Q int32, F fp32) factorisation of fp32 block scales.
     quant.py:52-96 (kernel), :99-140 (host).

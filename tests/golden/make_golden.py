@@ -22,6 +22,10 @@ The script re-executes itself with ``python -O`` because the reference's
 host wrappers ``assert tensor.is_cuda``; with ``-O`` those asserts are
 stripped and the same code runs on CPU tensors.
 
+  * ``_quantize_blockwise_int8`` of the reference's ``bench_int8_hybrid_moe.py``
+    (the weight preparation), taken out of that file with ``ast`` -- the file
+    itself imports the CUDA library at module level -- and run unchanged.
+
 Outputs ``tests/golden/*.npz``: routing maps, int8 activations, Q/F scales,
 scale offsets, GEMM outputs and the final output of each case, exactly as the
 reference code produced them.
@@ -354,13 +358,47 @@ def quant_cases(mods):
     return cases
 
 
+def weight_quant_cases(ref_root: Path, mods):
+    """The reference's weight preparation: blockwise INT8 weights
+    (bench_int8_hybrid_moe.py:98-120, block 64 x quant_block) and the hybrid
+    Q/F factorisation of their scales along K (:233-244)."""
+    import ast
+    src = (ref_root / "bench_int8_hybrid_moe.py").read_text()
+    fn = next(n for n in ast.parse(src).body
+              if isinstance(n, ast.FunctionDef) and n.name == "_quantize_blockwise_int8")
+    ns = {"torch": torch}
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), "bench_int8_hybrid_moe.py", "exec"), ns)
+    qblk = ns["_quantize_blockwise_int8"]
+    q = mods["quant"]
+    g = torch.Generator().manual_seed(4242)
+    cases = {}
+    for name, (E, N, K, sg) in {"wq_bf16_ragged": (3, 136, 200, 1),
+                                "wq_bf16_even": (2, 128, 512, 2)}.items():
+        w = (torch.randn(E, N, K, generator=g) * 0.02).to(torch.bfloat16)
+        w[1, :64, :128] = 0            # an all-zero block: the 1e-10 scale floor
+        w[0, 5, 7] = 0.5               # an outlier that owns its block's absmax
+        wq, scale = qblk(w, 64, 128)
+        Kb = scale.shape[-1]
+        Q, F = q.quantize_scales_for_hybrid(scale.reshape(-1, Kb).contiguous(), Q_max=16,
+                                            super_group_size=sg)
+        cases[name] = dict(w=_np(w), sg=np.int64(sg), q=wq.numpy(), scale=scale.numpy(),
+                           Q=Q.numpy().reshape(E, -1, Kb), F=F.numpy().reshape(E, -1, F.shape[-1]))
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", choices=["all", "weights"], default="all")
     args = ap.parse_args()
     mods = _load_reference(Path(args.ref))
     _keep = _register_ops()  # noqa: F841
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    if args.only == "weights":
+        for name, d in weight_quant_cases(Path(args.ref), mods).items():
+            np.savez_compressed(HERE / f"{name}.npz", **d)
+            print("wrote", name, {k: getattr(v, "shape", None) for k, v in d.items()})
+        return
     C = workloads.CONFIGS
     fwd = {
         "fwd_tiny": run_forward(mods, C["tiny"], True, True),
@@ -369,7 +407,7 @@ def main():
         "fwd_tm128": run_forward(mods, C["tm128"], True, True),
         "fwd_tiny_ep1of2": run_forward(mods, C["tiny"], True, True, ep=(1, 2)),
     }
-    for name, d in {**fwd, **quant_cases(mods)}.items():
+    for name, d in {**fwd, **quant_cases(mods), **weight_quant_cases(Path(args.ref), mods)}.items():
         np.savez_compressed(HERE / f"{name}.npz", **d)
         print("wrote", name, {k: getattr(v, "shape", None) for k, v in d.items()})
 

@@ -539,3 +539,30 @@ def test_router_fused_routing_matches_separate_calls(m, cname):
     for a, b in zip(fused[2:], sep):
         assert torch.equal(a, b)
     assert m._lib.device_error(0) == 0
+
+
+# ---------------------------------------------------------------------------
+# weight preparation (reference bench_int8_hybrid_moe.py:98-120, 228-244)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name", ["wq_bf16_ragged", "wq_bf16_even"])
+def test_weight_quant_golden(m, name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    w = torch.from_numpy(g["w"]).to(torch.bfloat16).to(DEV)
+    q, Q, F = m.quant.prepare_hybrid_weights(w, 16, int(g["sg"]))
+    _, scale = m.quant.quantize_weights_blockwise_int8(w)
+    np.testing.assert_array_equal(npf(q), g["q"])
+    np.testing.assert_array_equal(npf(scale), g["scale"])
+    np.testing.assert_array_equal(npf(Q), g["Q"])
+    np.testing.assert_array_equal(npf(F), g["F"])
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp16", "fp32"])
+def test_weight_quant_against_oracle_full_size(m, dt):
+    """A default-size w2 slab ([8, 2048, 512]) in each input type, bit-exact."""
+    g = torch.Generator().manual_seed(5)
+    w = (torch.randn(8, 2048, 512, generator=g) * 0.02).to(TDT[dt])
+    q, scale = m.quant.quantize_weights_blockwise_int8(w.to(DEV))
+    oq, os_ = ref.quantize_weights_blockwise(w.float().numpy(), 64, 128)
+    np.testing.assert_array_equal(npf(q), oq)
+    np.testing.assert_array_equal(npf(scale), os_)

@@ -88,3 +88,16 @@ def test_scale_factorisation_matches_reference_triton():
     Q, F = ref.quantize_scales_for_hybrid(g["s"], 16, 3)
     np.testing.assert_array_equal(Q, g["Q"])
     np.testing.assert_array_equal(F, g["F"])
+
+
+@pytest.mark.parametrize("name", ["wq_bf16_ragged", "wq_bf16_even"])
+def test_weight_quant_matches_reference_function(name):
+    """The weight preparation restated in the oracle equals the reference's own
+    _quantize_blockwise_int8 + quantize_scales_for_hybrid outputs."""
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    q, s = ref.quantize_weights_blockwise(g["w"], 64, 128)
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(s, g["scale"])
+    Q, F = ref.quantize_scales_for_hybrid(s.reshape(-1, s.shape[-1]), 16, int(g["sg"]))
+    np.testing.assert_array_equal(Q.reshape(g["Q"].shape), g["Q"])
+    np.testing.assert_array_equal(F.reshape(g["F"].shape), g["F"])
