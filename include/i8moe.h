@@ -288,6 +288,32 @@ int i8moe_int8_grouped_mm(const int8_t* a, const int8_t* b, void* out, int out_d
                           int64_t n_expert, int64_t sum_m, int64_t n, int64_t k,
                           i8moe_stream_t stream);
 
+/* ---------------------------------------------------- expert parallelism */
+/* No reference counterpart: the device-side bookkeeping of the expert-
+ * parallel dispatch and combine (the all-to-alls themselves are NCCL calls
+ * made by the host).  Rank d owns experts [d*n_local, (d+1)*n_local).
+ *
+ * ep_plan: for every token t and rank d, pos[t, d] = slot of t in d's send
+ *   segment (tokens in order) or -1; token_list [n_rank, n_token] holds each
+ *   segment's tokens; counts [n_rank] int32 the segment lengths. */
+int i8moe_ep_plan(const int32_t* topk_ids, int64_t n_token, int64_t topk, int64_t n_local_expert,
+                  int64_t n_rank, int32_t* pos, int32_t* token_list, int32_t* counts,
+                  i8moe_stream_t stream);
+/* ep_pack: rows of `hidden` (row_bytes each, a multiple of 16) of every
+ * segment, segment after segment, into send_rows; per row a meta row of its k
+ * ids followed by the bits of its k weights into send_meta [rows, 2k] int32.
+ * `counts` is a HOST array of the n_rank segment lengths. */
+int i8moe_ep_pack(const void* hidden, int64_t row_bytes, const int32_t* topk_ids,
+                  const float* topk_weights, int64_t topk, const int32_t* token_list,
+                  int64_t n_token, int64_t n_rank, const int64_t* counts, void* send_rows,
+                  int32_t* send_meta, i8moe_stream_t stream);
+/* ep_combine: out[t] = dtype(sum over ranks d in order of back[off_d +
+ * pos[t, d]]) with fp32 accumulation; back holds the returned partial rows
+ * segment by segment (HOST `counts` as for ep_pack). */
+int i8moe_ep_combine(const void* back, int dtype, const int32_t* pos, int64_t n_token,
+                     int64_t n_rank, const int64_t* counts, int64_t n_hidden, void* out,
+                     i8moe_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

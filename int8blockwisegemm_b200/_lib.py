@@ -23,6 +23,9 @@ I32 = c_int
 # name -> (restype, argtypes); must match include/i8moe.h exactly.
 PROTOTYPES = {
     "i8moe_abi_version": (I32, []),
+    "i8moe_ep_plan": (I32, [P, I64, I64, I64, I64, P, P, P, P]),
+    "i8moe_ep_pack": (I32, [P, I64, P, P, I64, P, I64, I64, P, P, P, P]),
+    "i8moe_ep_combine": (I32, [P, I32, P, I64, I64, P, I64, P, P]),
     "i8moe_last_error": (c_char_p, []),
     "i8moe_device_error": (I32, [I32, ctypes.POINTER(c_uint32), I32]),
     "i8moe_moe_permute_unpermute_supported": (I32, []),

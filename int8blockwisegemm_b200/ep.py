@@ -24,12 +24,18 @@ all-to-all:
   output agrees within the reference's tolerance rather than bit for bit.
 
 The all-to-alls are ``torch.distributed.all_to_all_single`` calls (NCCL over
-NVLink/NVSwitch on GPUs; gloo for the CPU tests).  Counts travel first; their
-host copy fixes the split sizes of the payload exchange, so a forward
-synchronises with the host once per dispatch.
+NVLink/NVSwitch on GPUs; gloo for the CPU tests).  On GPUs the bookkeeping
+around them runs in the library's kernels (csrc/ep.cu): a plan kernel gives
+every token its slot in each destination's segment, a pack kernel gathers the
+rows with their top-k ids and weights, and a combine kernel sums the returned
+partial rows.  The segment lengths of all ranks travel first (one all-gather)
+and their host copy sizes the payload exchange: one host synchronisation per
+dispatch.  Tensors on the CPU take an equivalent torch-only path.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 from dataclasses import dataclass
 from typing import Callable
@@ -48,6 +54,7 @@ class Dispatched:
     send_counts: list[int]      # rows sent to each rank
     recv_counts: list[int]      # rows received from each rank
     n_token: int                # local tokens
+    pos: torch.Tensor | None = None  # [n_token, P] slot in each send segment or -1 (GPU path)
 
 
 class ExpertParallel:
@@ -76,6 +83,8 @@ class ExpertParallel:
 
     def dispatch(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
                  topk_weights: torch.Tensor) -> Dispatched:
+        if hidden.is_cuda:
+            return self._dispatch_cuda(hidden, topk_ids, topk_weights)
         T, k = topk_ids.shape
         dev = hidden.device
         dest = topk_ids.long() // self.n_local                       # [T, k]
@@ -101,9 +110,47 @@ class ExpertParallel:
                   recv_counts, send_counts)
         return Dispatched(r_hidden, r_ids, r_w, send_idx, send_counts, recv_counts, T)
 
+    def _dispatch_cuda(self, hidden, topk_ids, topk_weights) -> Dispatched:
+        from ._lib import call
+        T, k = topk_ids.shape
+        K = hidden.shape[1]
+        dev, P = hidden.device, self.world
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        hidden = hidden.contiguous()
+        ids = topk_ids.to(torch.int32).contiguous()
+        wts = topk_weights.to(torch.float32).contiguous()
+        pos = torch.empty(T, P, dtype=torch.int32, device=dev)
+        lst = torch.empty(P, max(T, 1), dtype=torch.int32, device=dev)
+        counts = torch.empty(P, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            call("i8moe_ep_plan", ids.data_ptr(), T, k, self.n_local, P, pos.data_ptr(),
+                 lst.data_ptr(), counts.data_ptr(), stream)
+        allc = torch.empty(P * P, dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(allc, counts.to(torch.int64), group=self.group)
+        allc = allc.view(P, P).cpu()  # the one host synchronisation of the exchange
+        send_counts = allc[self.rank].tolist()
+        recv_counts = allc[:, self.rank].tolist()
+        n_send, n_recv = sum(send_counts), sum(recv_counts)
+        send_rows = torch.empty(n_send, K, dtype=hidden.dtype, device=dev)
+        send_meta = torch.empty(n_send, 2 * k, dtype=torch.int32, device=dev)
+        host_counts = (ctypes.c_int64 * P)(*send_counts)
+        with torch.cuda.device(dev):
+            call("i8moe_ep_pack", hidden.data_ptr(), K * hidden.element_size(), ids.data_ptr(),
+                 wts.data_ptr(), k, lst.data_ptr(), T, P, ctypes.addressof(host_counts),
+                 send_rows.data_ptr(), send_meta.data_ptr(), stream)
+        r_hidden = torch.empty(n_recv, K, dtype=hidden.dtype, device=dev)
+        r_meta = torch.empty(n_recv, 2 * k, dtype=torch.int32, device=dev)
+        self._a2a(r_hidden, send_rows, recv_counts, send_counts)
+        self._a2a(r_meta, send_meta, recv_counts, send_counts)
+        r_ids = r_meta[:, :k].contiguous()
+        r_w = r_meta[:, k:].contiguous().view(torch.float32)
+        return Dispatched(r_hidden, r_ids, r_w, None, send_counts, recv_counts, T, pos)
+
     def combine(self, d: Dispatched, partial: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         """Return the partial rows to their sources and sum them per token."""
+        if partial.is_cuda and d.pos is not None:
+            return self._combine_cuda(d, partial, out)
         K = partial.shape[1]
         back = torch.empty(sum(d.send_counts), K, dtype=partial.dtype, device=partial.device)
         self._a2a(back, partial.contiguous(), d.send_counts, d.recv_counts)
@@ -116,6 +163,22 @@ class ExpertParallel:
         if out is None:
             return acc.to(partial.dtype)
         out.copy_(acc)
+        return out
+
+    def _combine_cuda(self, d: Dispatched, partial: torch.Tensor, out):
+        from ._lib import BF16, FP16, call
+        K = partial.shape[1]
+        dev, P = partial.device, self.world
+        back = torch.empty(sum(d.send_counts), K, dtype=partial.dtype, device=dev)
+        self._a2a(back, partial.contiguous(), d.send_counts, d.recv_counts)
+        if out is None:
+            out = torch.empty(d.n_token, K, dtype=partial.dtype, device=dev)
+        host_counts = (ctypes.c_int64 * P)(*d.send_counts)
+        dt = {torch.bfloat16: BF16, torch.float16: FP16}[partial.dtype]
+        with torch.cuda.device(dev):
+            call("i8moe_ep_combine", back.data_ptr(), dt, d.pos.data_ptr(), d.n_token, P,
+                 ctypes.addressof(host_counts), K, out.data_ptr(),
+                 torch.cuda.current_stream(dev).cuda_stream)
         return out
 
     def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,

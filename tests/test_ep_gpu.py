@@ -77,6 +77,9 @@ def _worker(rank, world, port, cfg_name, errq):
             fa, fb = int(feo[e]), int(feo[e + 1])
             assert b - a == fb - fa, f"expert {e}: {b - a} rows vs {fb - fa}"
             for name in ("a1q", "mm1", "a2q", "mm2"):
+                if tr[name] is None:  # mm1 is not materialised by the fused w13 epilogue
+                    assert full_tr[name] is None
+                    continue
                 assert torch.equal(tr[name][a:b], full_tr[name][fa:fb]), f"{name} of expert {e}"
         assert pkg._lib.device_error(rank) == 0
         dist.barrier()
