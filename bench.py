@@ -264,16 +264,27 @@ def make_problem(cfg, inp, dev):
 
 
 def time_w13_gemm(pkg, cfg, st, tr, iters=20):
-    """Average device time of the w13 grouped GEMM launch (dominant kernel),
-    CUDA events on the launching stream."""
+    """Average device time of the w13 grouped GEMM launch (dominant kernel) as
+    the forward runs it -- with the SiLU*up + requant epilogue when the trace
+    shows the fused path (no mm1) -- CUDA events on the launching stream."""
     tm = tr["tile_m"]
-    fn = (pkg.ops.cutlass_int8_blockwise_hybrid_grouped if tm == 128
-          else pkg.ops.cutlass_int8_blockwise_hybrid_grouped_small)
     R = tr["a1q"].shape[0]
-    out = st["workspace13"].flatten()[: R * 2 * cfg.N].view(R, 2 * cfg.N)
-    args = (tr["a1q"], tr["a1_Q"], tr["a1_F"], st["w1"], st["w1_qscale"], st["w1_fscale"],
-            tr["expert_offsets"], tr["problem_sizes1"], out, cfg.quant_block, cfg.sg,
-            tr["a1_so"])
+    if tr["mm1"] is None:
+        so = tr["scale_offsets"] if tr.get("scale_offsets") is not None else tr["a1_so"]
+        dt = {"bf16": torch.bfloat16, "fp16": torch.float16}[cfg.dtype]
+
+        def fn(*a):
+            pkg.quant.fused_w13_silu_quant_int8_hybrid_grouped(*a)
+        args = (tr["a1q"], tr["a1_Q"], tr["a1_F"], st["w1"], st["w1_qscale"], st["w1_fscale"],
+                tr["expert_offsets"], tr["problem_sizes1"], so, cfg.quant_block, cfg.q_max,
+                cfg.sg, tm, dt)
+    else:
+        fn = (pkg.ops.cutlass_int8_blockwise_hybrid_grouped if tm == 128
+              else pkg.ops.cutlass_int8_blockwise_hybrid_grouped_small)
+        out = st["workspace13"].flatten()[: R * 2 * cfg.N].view(R, 2 * cfg.N)
+        args = (tr["a1q"], tr["a1_Q"], tr["a1_F"], st["w1"], st["w1_qscale"], st["w1_fscale"],
+                tr["expert_offsets"], tr["problem_sizes1"], out, cfg.quant_block, cfg.sg,
+                tr["a1_so"])
     for _ in range(3):
         fn(*args)
     torch.cuda.synchronize()
@@ -294,6 +305,29 @@ def time_w13_gemm(pkg, cfg, st, tr, iters=20):
     torch.cuda.synchronize()
     del g
     return e0.elapsed_time(e1) / iters * 1e-3
+
+
+def w13_algorithmic_bytes(cfg, tr):
+    """Algorithmic HBM bytes of one w13 launch: int8 A rows, the int8 weights of
+    the experts that have rows, their Q/F scales, and the output -- int8 a2q
+    with its Q/F when SiLU*up + requant is fused into the epilogue, else the
+    16-bit [R, 2N] mm1."""
+    eft = tr["eft"].cpu()
+    R = int(eft[-1])
+    e_hit = int(((eft[1:] - eft[:-1]) > 0).sum())
+    tm = tr["tile_m"]
+    kb = -(-cfg.K // cfg.quant_block)
+    kb_sg = -(-kb // cfg.sg)
+    n_sb = -(-2 * cfg.N // 64)
+    rows_s = int(((eft[1:] - eft[:-1]) + tm - 1).div(tm, rounding_mode="floor").sum())
+    b = R * cfg.K + e_hit * 2 * cfg.N * cfg.K              # A, W
+    b += e_hit * n_sb * (kb + kb_sg) * 4 + rows_s * (kb + kb_sg) * 4  # W and A Q/F
+    if tr["mm1"] is None:
+        nb = -(-cfg.N // cfg.quant_block)
+        b += R * cfg.N + rows_s * (nb + -(-nb // cfg.sg)) * 4   # a2q and its Q/F
+    else:
+        b += R * 2 * cfg.N * 2                                   # mm1
+    return b
 
 
 def run_ours_ep(args, world, rank, local):
@@ -385,12 +419,7 @@ def run_ours_ep(args, world, rank, local):
     st = {"w1": moe.w1, "w1_qscale": moe.w1_q, "w1_fscale": moe.w1_f,
           "workspace13": torch.empty(R_buf * 2 * cfg.N, dtype=hidden.dtype, device=dev)}
     t_gemm = max_over_ranks(time_w13_gemm(pkg, cfg, st, tr), world)
-    eft = tr["eft"].cpu()
-    R_loc = int(eft[-1])
-    e_hit = int(((eft[1:] - eft[:-1]) > 0).sum())
-    n_sb, kb = -(-2 * cfg.N // 64), -(-cfg.K // 128)
-    gemm_bytes = (R_loc * cfg.K + e_hit * 2 * cfg.N * cfg.K + R_loc * 2 * cfg.N * 2
-                  + e_hit * n_sb * kb * 4 * 2 + tr["a1_Q"].shape[0] * kb * 4)
+    gemm_bytes = w13_algorithmic_bytes(cfg, tr)
     hbm, _, src = measured_peaks()
     achieved = gemm_bytes / t_gemm / 1e9
     line = {
@@ -408,7 +437,7 @@ def run_ours_ep(args, world, rank, local):
                    "timing": "eager EP forward (dispatch sizes come from host-side counts), "
                              "CUDA events, max over ranks"},
         "clocks": clocks,
-        "gpu_launches": 8 * args.steps,
+        "gpu_launches": 12 * args.steps,  # ep_plan, ep_pack, ep_combine + the 9 of the local forward
         "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel (w13, local experts)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": src, "traffic": None, "algorithmic_bytes": gemm_bytes,
@@ -506,22 +535,17 @@ def run_ours(args, world, rank, local):
     fwd(_trace=tr)
     torch.cuda.synchronize()
     t_gemm = time_w13_gemm(pkg, cfg, st, tr)
-    eft = tr["eft"].cpu()
-    e_hit = int(((eft[1:] - eft[:-1]) > 0).sum())
-    n_sb = -(-2 * cfg.N // 64)
-    kb = -(-cfg.K // 128)
-    rows_s = tr["a1_Q"].shape[0]
-    gemm_bytes = (R * cfg.K + e_hit * 2 * cfg.N * cfg.K + R * 2 * cfg.N * 2
-                  + e_hit * n_sb * kb * 4 * 2 + rows_s * kb * 4)
+    gemm_bytes = w13_algorithmic_bytes(cfg, tr)
     gemm_ops = 2 * R * 2 * cfg.N * cfg.K
     hbm, bf16, src = measured_peaks()
     achieved = gemm_bytes / t_gemm / 1e9
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get(f"{cfg.name}/w13_gemm")
+        key = "w13_gemm_silu_quant" if tr["mm1"] is None else "w13_gemm"
+        traffic = json.loads(tfile.read_text()).get(f"{cfg.name}/{key}")
 
-    gpu_launches = 8 * args.steps
+    gpu_launches = 9 * args.steps  # route x3, quant, scales_to_qf x2, w13, w2, unpermute
     line = {
         "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -536,7 +560,8 @@ def run_ours(args, world, rank, local):
                    "timing": "CUDA-graph replay of the whole forward, CUDA events, max over ranks"},
         "clocks": clocks,
         "gpu_launches": gpu_launches,
-        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel (w13)",
+        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel (w13"
+                     + (", SiLU*up + requant epilogue)" if tr["mm1"] is None else ")"),
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": src, "traffic": traffic,
                      "algorithmic_bytes": gemm_bytes, "launch_ms": t_gemm * 1e3,

@@ -188,7 +188,7 @@ def _run_cutlass_int8_hybrid_grouped_moe(
             problem_sizes1=problem_sizes1, problem_sizes2=problem_sizes2, tile_m=tile_m,
             a1q=a1q, a1_Q=a1_qscale, a1_F=a1_fscale, a1_so=a1_scale_offsets,
             mm1=None if fuse_w13 else mm1_out.clone(), a2q=a2q, a2_Q=a2_qscale, a2_F=a2_fscale, a2_so=a2_scale_offsets,
-            mm2=mm2_out.clone())
+            mm2=mm2_out.clone(), scale_offsets=scale_offsets)
         if _USE_FUSED_PERMUTE_QUANT_W1:
             _trace["pidx"] = permuted_idx
 
