@@ -288,6 +288,15 @@ int i8moe_int8_grouped_mm(const int8_t* a, const int8_t* b, void* out, int out_d
                           int64_t n_expert, int64_t sum_m, int64_t n, int64_t k,
                           i8moe_stream_t stream);
 
+/* Grouped-GEMM variant (no reference counterpart; results are identical
+ * either way).  mode 1: every hybrid grouped GEMM above runs on CTA pairs --
+ * clusters of two CTAs sharing one tcgen05.mma.cta_group::2 over 256-row
+ * pair tiles of one expert, each CTA streaming half of the weight tile;
+ * mode 0 and mode -1 (default): one CTA per 128-row tile (measured faster
+ * at the benchmark shapes).  Process-wide; returns the previous mode, or
+ * I8MOE_ERR_INVALID for another value. */
+int i8moe_gemm_set_cta_pairs(int mode);
+
 /* ---------------------------------------------------- expert parallelism */
 /* No reference counterpart: the device-side bookkeeping of the expert-
  * parallel dispatch and combine (the all-to-alls themselves are NCCL calls

@@ -55,6 +55,7 @@ PROTOTYPES = {
                                                    I64, I64, I64, I64, I64, I64, I64, I64, P, P,
                                                    P, P]),
     "i8moe_int8_grouped_mm": (I32, [P, P, P, I32, c_float, P, P, P, P, I64, I64, I64, I64, P]),
+    "i8moe_gemm_set_cta_pairs": (I32, [I32]),
 }
 
 BF16, FP16, FP32, S32 = 0, 1, 2, 3
@@ -90,6 +91,15 @@ def check(rc: int, what: str = "") -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(LIB, name)(*args), name)
+
+
+def set_cta_pairs(mode: int) -> int:
+    """Grouped-GEMM variant: 1 CTA pairs (cta_group::2), 0 one CTA per tile,
+    -1 by problem shape (default).  Returns the previous mode."""
+    prev = _load().i8moe_gemm_set_cta_pairs(int(mode))
+    if prev < -1:
+        check(prev, "i8moe_gemm_set_cta_pairs")
+    return prev
 
 
 def device_error(device: int, clear: bool = False) -> int:

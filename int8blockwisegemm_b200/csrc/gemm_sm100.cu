@@ -70,15 +70,26 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 128;  // bytes == int8 elements per K-tile
-constexpr int STAGES = 3;
 constexpr int NACC = 2;
 constexpr int kEpiWarps = 16;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue warps
 constexpr int kMaxExperts = 1024;
 constexpr int kTileABytes = BM * BK;
-constexpr int kTileBBytes = BN * BK;
 constexpr uint32_t kTmemCols = NACC * BN;
-constexpr uint32_t kIdesc = idesc_i8(BM, BN);
+constexpr int kSmemLimit = 227 * 1024;  // dynamic shared memory per CTA on sm_100
+
+// CG = 1: one CTA per 128 x 256 tile (tcgen05.mma.cta_group::1, M = 128),
+//   every CTA streams A [128 x 128] and all of B [256 x 128] per K-tile.
+// CG = 2: a cluster of two CTAs per 256 x 256 pair tile (cta_group::2,
+//   M = 256): each CTA streams its own A rows and half of the B rows
+//   (32 KB per K-tile instead of 48 KB), so the ring is five stages deep.
+template <int CG>
+struct Cfg {
+  static constexpr int kStages = CG == 2 ? 5 : 3;
+  static constexpr int kBRows = BN / CG;  // B rows this CTA loads per K-tile
+  static constexpr int kTileBBytes = kBRows * BK;
+  static constexpr uint32_t kIdesc = idesc_i8(BM * CG, BN);
+};
 
 enum GemmMode { kHybrid = 0, kPerTensor = 1 };
 // Epilogue: store the scaled product, or (w13 only) SiLU(gate)*up + INT8
@@ -112,16 +123,18 @@ struct GemmParams {
   int kb_act;
 };
 
+template <int CG>
 struct SmemLayout {
+  static constexpr int kStages = Cfg<CG>::kStages;
   static constexpr int kA = 0;
-  static constexpr int kB = kA + STAGES * kTileABytes;
+  static constexpr int kB = kA + kStages * kTileABytes;
   // per-epilogue-warp output staging (32 rows x 64 B, 64-byte swizzle)
-  static constexpr int kStg = kB + STAGES * kTileBBytes;  // 1024-B aligned
+  static constexpr int kStg = kB + kStages * Cfg<CG>::kTileBBytes;  // 1024-B aligned
   static constexpr int kStgWarpBytes = 32 * 64;
   static constexpr int kBar = kStg + kEpiWarps * kStgWarpBytes;  // 8-B aligned
   // full/empty ring, accumulator full/empty, final drain, and the two
   // row-group absmax barriers of the fused SiLU-quant epilogue
-  static constexpr int kNumBars = 2 * STAGES + 2 * NACC + 1 + 2;
+  static constexpr int kNumBars = 2 * kStages + 2 * NACC + 1 + 2;
   static constexpr int kMisc = kBar + kNumBars * 8;   // tmem base, abort flag
   static constexpr int kRed = kMisc + 16;             // absmax slots [2 groups][3]
   // per-epilogue-thread slots (Q_A, Q_B, Q_B(up) per tile parity; F_A, F_B,
@@ -203,11 +216,25 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const int* mt_prefix, int
   return ti;
 }
 
-template <int MODE, bool HAS_BIAS, typename OutT, int EPI>
+// the tile's coordinates as seen by this CTA: with CTA pairs, mt_prefix
+// counts pair tiles and the CTA of rank r owns m-tile 2 * (pair m-tile) + r
+template <int CG>
+__device__ __forceinline__ TileInfo decode_tile_cta(int t, const int* mt_prefix, int E,
+                                                    int n_tiles, int rank) {
+  TileInfo ti = decode_tile(t, mt_prefix, E, n_tiles);
+  if (CG == 2) ti.mt = 2 * ti.mt + rank;
+  return ti;
+}
+
+template <int MODE, bool HAS_BIAS, typename OutT, int EPI, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
+  using SmemLayout = i8moe::SmemLayout<CG>;
+  constexpr int STAGES = Cfg<CG>::kStages;
+  constexpr int kTileBBytes = Cfg<CG>::kTileBBytes;
+  constexpr uint32_t kIdesc = Cfg<CG>::kIdesc;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -232,9 +259,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- prologue: per-expert tables (tile prefix, scale rows, rows) ----
   // Kept in shared memory so a tile's coordinates resolve without global
   // loads on the epilogue's critical path.
+  // Tiles are enumerated per CTA pair when CG == 2: mt_prefix then counts
+  // pair tiles (two 128-row m-tiles each), and a CTA's own m-tile is
+  // 2 * (pair m-tile) + its rank in the pair.
+  const int rank = CG == 2 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int tile0 = CG == 2 ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int tstride = CG == 2 ? static_cast<int>(cluster_count_x()) : static_cast<int>(gridDim.x);
   for (int e = threadIdx.x; e < p.E; e += kThreads) {
     const int m = max(0, __ldg(p.ps + 3 * e));
-    mt_prefix[e] = (m + BM - 1) / BM;
+    mt_prefix[e] = CG == 2 ? ((m + BM - 1) / BM + 1) / 2 : (m + BM - 1) / BM;
     so_prefix[e] = p.so ? __ldg(p.so + e) : (m + p.tile_m - 1) / p.tile_m;
     m_rows[e] = m;
     e_row0[e] = __ldg(p.eo + e);
@@ -253,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(bar_accf + 8 * a, 1);
-      mbar_init(bar_acce + 8 * a, kEpiWarps);
+      mbar_init(bar_acce + 8 * a, CG * kEpiWarps);  // both CTAs' epilogues release
     }
     mbar_init(bar_final, 1);
     // absmax groups: all 16 epilogue warps (tile_m 128) or the 8 warps of
@@ -262,14 +295,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_red + 8, p.tile_m == 64 ? kEpiWarps / 2 : kEpiWarps);
     mbar_fence_init();
   }
+  // the other CTA of a pair signals this CTA's barriers: they must be
+  // initialised before either CTA goes on
+  if constexpr (CG == 2) cluster_sync();
   if (warp == 1) {
-    tmem_alloc(smem_u32(s_tmem), kTmemCols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(smem_u32(s_tmem), kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(s_tmem), kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
+  // the pair's first CTA holds the ring's full barriers and the accumulator
+  // empty barriers that both CTAs signal
+  const uint32_t full0 = CG == 2 ? mapa_shared(bar_full, 0) : bar_full;
+  const uint32_t acce0 = CG == 2 ? mapa_shared(bar_acce, 0) : bar_acce;
 
   if (warp == 0) {
     // ================= TMA producer =================
@@ -283,10 +328,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+      for (int t = tile0; t < total_tiles && ok; t += tstride) {
+        const TileInfo ti = decode_tile_cta<CG>(t, mt_prefix, p.E, p.n_tiles, rank);
         const int row0 = e_row0[ti.e] + ti.mt * BM;
         const int n0 = ti.nt * (EPI == kEpiSiluQuant ? 128 : BN);
+        // CG == 2: an expert with an odd number of m-tiles leaves one CTA of
+        // its last pair tile without rows; that CTA loads no A (its
+        // accumulator rows are discarded) but still its half of B.
+        const int mt_e = (m_rows[ti.e] + BM - 1) / BM;
+        const bool own_ok = ti.mt < mt_e;
+        const bool peer_ok = CG == 2 && (ti.mt ^ 1) < mt_e;
+        const uint32_t tx = CG == 2 ? (own_ok + peer_ok) * kTileABytes + 2 * kTileBBytes
+                                    : kTileABytes + kTileBBytes;
+        // this CTA's B rows: store epilogue [n0 + 128*rank, +128) of the
+        // tile; fused SiLU epilogue gate rows [n0, +128) (first CTA) and the
+        // matching up rows [n_act + n0, +128) (second CTA)
+        const int b_row = EPI == kEpiSiluQuant ? (rank ? p.n_act + n0 : n0) : n0 + 128 * rank;
         for (int kt = 0; kt < p.kt_total; ++kt) {
           if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, s_abort, &g_err_gemm,
                          kErrProducerTimeout)) {
@@ -294,24 +351,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const int kx = kt * BK - p.k_pad;
-          const uint32_t fb = bar_full + 8 * stage;
           const uint32_t b_dst = sbase + SmemLayout::kB + stage * kTileBBytes;
-          mbar_arrive_expect_tx(fb, kTileABytes + kTileBBytes);
-          tma_load_2d(sbase + SmemLayout::kA + stage * kTileABytes, &tmA, fb, kx, row0);
-          if (EPI == kEpiSiluQuant) {
-            // gate rows [n0, n0+128) and the matching up rows [n_act+n0, +128)
-            tma_load_3d(b_dst, &tmB, fb, kx, n0, ti.e);
-            tma_load_3d(b_dst + kTileBBytes / 2, &tmB, fb, kx, p.n_act + n0, ti.e);
+          const uint32_t a_dst = sbase + SmemLayout::kA + stage * kTileABytes;
+          if constexpr (CG == 2) {
+            if (rank == 0) mbar_arrive_expect_tx(bar_full + 8 * stage, tx);
+            const uint32_t fb = full0 + 8 * stage;
+            if (own_ok) tma_load_2d_pair(a_dst, &tmA, fb, kx, row0);
+            tma_load_3d_pair(b_dst, &tmB, fb, kx, b_row, ti.e);
           } else {
-            tma_load_3d(b_dst, &tmB, fb, kx, n0, ti.e);
+            const uint32_t fb = bar_full + 8 * stage;
+            mbar_arrive_expect_tx(fb, tx);
+            tma_load_2d(a_dst, &tmA, fb, kx, row0);
+            if (EPI == kEpiSiluQuant) {
+              // gate rows [n0, n0+128) and the matching up rows [n_act+n0, +128)
+              tma_load_3d(b_dst, &tmB, fb, kx, n0, ti.e);
+              tma_load_3d(b_dst + kTileBBytes / 2, &tmB, fb, kx, p.n_act + n0, ti.e);
+            } else {
+              tma_load_3d(b_dst, &tmB, fb, kx, b_row, ti.e);
+            }
           }
           issued[stage] = true;
           issued_phase[stage] = phase;
           if (++stage == STAGES) stage = 0, phase ^= 1;
         }
       }
-      if (!ok) {
+      if (CG == 2 && ok) {
+        // the first CTA's MMA commits arrive on this CTA's empty barriers:
+        // wait for the last one of every stage before the CTA may exit
+        for (int s = 0; s < STAGES && ok; ++s) {
+          ok = mbar_wait(bar_empty + 8 * stage, phase ^ 1, s_abort, &g_err_gemm,
+                         kErrProducerTimeout);
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+      if (!ok && (CG == 1 || rank == 0)) {
         // drain: never exit with TMA writes into this CTA's smem in flight
+        // (a pair's second CTA counts its copies on the first CTA's
+        // barriers, which the first CTA drains for both)
         volatile int no_abort = 0;
         for (int s = 0; s < STAGES; ++s)
           if (issued[s])
@@ -321,21 +397,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ================= MMA issuer =================
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t aphase = 0;
       bool ok = true;
       bool any = false;
+      // a pair MMA frees the stage and fills the accumulator in both CTAs
+      const uint32_t empty1 = CG == 2 ? mapa_shared(bar_empty, 1) : 0u;
+      const uint32_t accf1 = CG == 2 ? mapa_shared(bar_accf, 1) : 0u;
+      const uint32_t empty0 = CG == 2 ? mapa_shared(bar_empty, 0) : bar_empty;
+      const uint32_t accf0 = CG == 2 ? mapa_shared(bar_accf, 0) : bar_accf;
       // The issuer needs no tile coordinates: it walks this CTA's quant
-      // blocks in order (tiles blockIdx.x, +gridDim.x, ...), one TMEM
+      // blocks in order (tiles tile0, +tstride, ...), one TMEM
       // accumulator buffer per block.  Shared memory filled by TMA is made
       // visible by the full-barrier wait itself; the tcgen05 fence is only
       // needed after the accumulator hand-back, which the epilogue's
       // tcgen05.ld precede.
-      const int my_tiles =
-          blockIdx.x < total_tiles ? (total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const int my_tiles = tile0 < total_tiles ? (total_tiles - 1 - tile0) / tstride + 1 : 0;
       const int n_blocks = my_tiles * p.nq;
       int qb = 0;
       for (int i = 0; i < n_blocks; ++i) {
@@ -358,20 +438,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < BK / 32; ++k) {
             const uint64_t ad = sw128_kmajor_desc(a_addr + k * 32);
             const uint64_t bd = sw128_kmajor_desc(b_addr + k * 32);
-            umma_i8(d_tmem, ad, bd, kIdesc, (kt > kt0 || k > 0) ? 1u : 0u);
+            if constexpr (CG == 2)
+              umma_i8_pair(d_tmem, ad, bd, kIdesc, (kt > kt0 || k > 0) ? 1u : 0u);
+            else
+              umma_i8(d_tmem, ad, bd, kIdesc, (kt > kt0 || k > 0) ? 1u : 0u);
           }
           any = true;
-          umma_commit(bar_empty + 8 * stage);
+          if constexpr (CG == 2) {
+            umma_commit_pair(empty0 + 8 * stage);
+            umma_commit_pair(empty1 + 8 * stage);
+          } else {
+            umma_commit(bar_empty + 8 * stage);
+          }
           if (++stage == STAGES) stage = 0, phase ^= 1;
         }
         if (!ok) break;
-        umma_commit(bar_accf + 8 * acc);
+        if constexpr (CG == 2) {
+          umma_commit_pair(accf0 + 8 * acc);
+          umma_commit_pair(accf1 + 8 * acc);
+        } else {
+          umma_commit(bar_accf + 8 * acc);
+        }
         if (++acc == NACC) acc = 0, aphase ^= 1;
         if (++qb == p.nq) qb = 0;
       }
       // wait for every issued MMA before TMEM can be released
       if (any) {
-        umma_commit(bar_final);
+        if constexpr (CG == 2)
+          umma_commit_pair(mapa_shared(bar_final, 0));
+        else
+          umma_commit(bar_final);
         volatile int no_abort = 0;
         mbar_wait(bar_final, 0, &no_abort, &g_err_gemm, kErrDrainTimeout, 200000000ull);
       }
@@ -429,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Q_A * Q_B of quant block (qb0 + lane) of tile t, synchronously (only
     // for more than 32 quant blocks); `up` selects the up half when fused
     auto tile_q = [&](int t, int qb0, bool up) -> int {
-      const TileInfo u = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+      const TileInfo u = decode_tile_cta<CG>(t, mt_prefix, p.E, p.n_tiles, rank);
       const int wrow = u.mt * BM + quad * 32;
       const int col = first_col(u);
       const int qb = qb0 + lane;
@@ -445,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t s_qa = s_slot + (3 * par) * kSA, s_qb = s_qa + kSA, s_qbu = s_qb + kSA;
       bool any = false;
       if (MODE == kHybrid && t < total_tiles) {
-        const TileInfo u = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+        const TileInfo u = decode_tile_cta<CG>(t, mt_prefix, p.E, p.n_tiles, rank);
         const int wrow = u.mt * BM + quad * 32;
         const int col = first_col(u);
         const int qb = lane;
@@ -464,10 +560,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kFused) st_s32(s_qbu, 0);
       }
     };
-    fetch_q(blockIdx.x, 0);
+    fetch_q(tile0, 0);
     int par = 0;
-    int lt = 0;  // local tile counter (absmax barrier phase and slots)
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, par ^= 1, ++lt) {
+    int lt = 0;  // fused epilogues run so far (absmax barrier phase and slots)
+    for (int t = tile0; t < total_tiles && ok; t += tstride, par ^= 1) {
       cp_async_wait_all();
       int qv, qvu = 0;
       {
@@ -476,10 +572,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         qv = qa * ld_s32(s_qa + kSA);
         if (kFused) qvu = qa * ld_s32(s_qa + 2 * kSA);
       }
-      fetch_q(t + gridDim.x, par ^ 1);
+      fetch_q(t + tstride, par ^ 1);
+      // CG == 2: this CTA's half of the pair tile may lie past the expert's
+      // rows; its accumulator is then released unread and nothing is stored
+      const TileInfo tc = decode_tile_cta<CG>(t, mt_prefix, p.E, p.n_tiles, rank);
+      const bool own_ok = CG == 1 || tc.mt * BM < m_rows[tc.e];
       {
         // F_A, F_B (, F_B of the up half) of this tile, for the output phase
-        const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+        const TileInfo& ti = tc;
         const int wrow0 = ti.mt * BM + quad * 32;
         const int col0 = first_col(ti);
         if (MODE == kHybrid && wrow0 < m_rows[ti.e] && col_valid(col0)) {
@@ -511,6 +611,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        if (!own_ok) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acce0 + 8 * acc);
+          if (++acc == NACC) acc = 0, aphase ^= 1;
+          continue;
+        }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           tmem_ld16(tmem_base + t_lane + acc * BN + chunk_col(c), P);
@@ -518,7 +625,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c == 3) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acce + 8 * acc);
+            if (lane == 0) {
+              if constexpr (CG == 2)
+                mbar_arrive_cluster(acce0 + 8 * acc);
+              else
+                mbar_arrive(bar_acce + 8 * acc);
+            }
             if (++acc == NACC) acc = 0, aphase ^= 1;
           }
           if (MODE == kHybrid) {
@@ -532,7 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      const TileInfo ti = decode_tile(t, mt_prefix, p.E, p.n_tiles);
+      if (!own_ok) continue;
+      const TileInfo& ti = tc;
       const int m_e = m_rows[ti.e];
       const int wrow0 = ti.mt * BM + quad * 32;
       const int lrow = wrow0 + lane;
@@ -641,6 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (col0 + 8 * j < p.n_act)
               *reinterpret_cast<uint2*>(dst + 8 * j) = make_uint2(qw[2 * j], qw[2 * j + 1]);
         }
+        ++lt;
         continue;
       }
       // ---- convert, scale, round, store ----
@@ -737,9 +851,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves while the other may still signal its
+  // barriers or the pair MMA may still read its shared memory
+  if constexpr (CG == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -822,20 +942,93 @@ int make_tmap_act(CUtensorMap* m, int8_t* act, int64_t rows, int64_t n_act) {
   return I8MOE_OK;
 }
 
+// Launches one instantiation persistently: one CTA per SM (CG == 1) or as
+// many CTA pairs as can be resident at once (CG == 2, clusters of two), never
+// more than there are tiles.
+template <int MODE, bool HAS_BIAS, typename OutT, int EPI, int CG>
+int launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+              const GemmParams& p, int64_t upper_tiles, cudaStream_t st) {
+  auto kern = grouped_gemm_kernel<MODE, HAS_BIAS, OutT, EPI, CG>;
+  const int smem = SmemLayout<CG>::bytes(p.E) + 1024;
+  const int smem_max = std::min(SmemLayout<CG>::bytes(kMaxExperts) + 1024, kSmemLimit);
+  if (smem > smem_max) return set_error(I8MOE_ERR_UNSUPPORTED, "grouped GEMM: too many experts");
+  static int attr_done[64] = {0};
+  static int max_clusters[64] = {0};
+  const int dev = current_device();
+  const bool cached = dev >= 0 && dev < 64 && __atomic_load_n(&attr_done[dev], __ATOMIC_ACQUIRE);
+  int n_pairs = 0;
+  if (!cached) {
+    I8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
+    if (CG == 2) {
+      cudaLaunchConfig_t q = {};
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 2;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.gridDim = dim3(2 * static_cast<unsigned>(num_sms(dev) / 2));
+      q.blockDim = dim3(kThreads);
+      q.dynamicSmemBytes = smem_max;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      I8_CUDA(cudaOccupancyMaxActiveClusters(&n_pairs, kern, &q));
+      if (n_pairs < 1) return set_error(I8MOE_ERR_UNSUPPORTED, "no CTA pair fits on the device");
+    }
+    if (dev >= 0 && dev < 64) {
+      __atomic_store_n(&max_clusters[dev], n_pairs, __ATOMIC_RELAXED);
+      __atomic_store_n(&attr_done[dev], 1, __ATOMIC_RELEASE);
+    }
+  } else {
+    n_pairs = __atomic_load_n(&max_clusters[dev], __ATOMIC_RELAXED);
+  }
+  if constexpr (CG == 2) {
+    const int pairs = static_cast<int>(std::min<int64_t>(n_pairs, std::max<int64_t>(upper_tiles, 1)));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(pairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    I8_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, p));
+  } else {
+    const int grid = static_cast<int>(std::min<int64_t>(num_sms(dev), std::max<int64_t>(upper_tiles, 1)));
+    kern<<<grid, kThreads, smem, st>>>(ta, tb, to, p);
+  }
+  return check_launch("grouped_gemm_kernel");
+}
+
+// CTA pairs: -1 chooses by problem shape, 0 never, 1 always (hybrid GEMMs).
+int g_cta_pairs = -1;
+
+// the pair layout's five-stage ring leaves room for the per-expert tables
+// of up to ~700 experts within the 227 KB a CTA may use
+bool pairs_fit(int64_t E) { return SmemLayout<2>::bytes(static_cast<int>(E)) + 1024 <= kSmemLimit; }
+
+// Pair tiles cover 256 rows of one expert, so an expert with an odd number
+// of 128-row m-tiles leaves half of its last pair tile idle.  Measured on
+// B200 at the benchmark shapes, a pair tile's quant block takes as long as a
+// single CTA's (~1.2-1.3 k cycles: the epilogue's instruction issue, not the
+// 48 KB operand stream, bounds it), so the idle halves make pairs slower;
+// the default (-1) is therefore one CTA per tile, and pairs are opt-in.
+bool use_cta_pairs(int mode, int64_t sum_m, int64_t E) {
+  (void)sum_m;
+  if (mode != kHybrid || !pairs_fit(E)) return false;
+  return __atomic_load_n(&g_cta_pairs, __ATOMIC_RELAXED) == 1;
+}
+
 template <int MODE, bool HAS_BIAS, typename OutT, int EPI = kEpiStore>
 int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-             const GemmParams& p, int grid, cudaStream_t st) {
-  auto kern = grouped_gemm_kernel<MODE, HAS_BIAS, OutT, EPI>;
-  const int smem = SmemLayout::bytes(p.E) + 1024;
-  static int attr_done[64] = {0};
-  const int dev = current_device();
-  if (dev < 0 || dev >= 64 || !__atomic_load_n(&attr_done[dev], __ATOMIC_ACQUIRE)) {
-    I8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 SmemLayout::bytes(kMaxExperts) + 1024));
-    if (dev >= 0 && dev < 64) __atomic_store_n(&attr_done[dev], 1, __ATOMIC_RELEASE);
+             const GemmParams& p, int64_t upper_tiles, bool pairs, cudaStream_t st) {
+  if constexpr (MODE == kHybrid) {
+    if (pairs) return launch_cg<MODE, HAS_BIAS, OutT, EPI, 2>(ta, tb, to, p, upper_tiles, st);
   }
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, to, p);
-  return check_launch("grouped_gemm_kernel");
+  return launch_cg<MODE, HAS_BIAS, OutT, EPI, 1>(ta, tb, to, p, upper_tiles, st);
 }
 
 int check_device() {
@@ -879,10 +1072,13 @@ int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const i
   if (rc) return rc;
   rc = get_encode();
   if (rc) return rc;
+  const bool pairs = use_cta_pairs(mode, sum_m, E);
   CUtensorMap ta, tb;
   rc = make_tmap_a(&ta, a, sum_m, k);
   if (rc) return rc;
-  rc = make_tmap_b(&tb, b, E, n, k, epi == kEpiSiluQuant ? 128 : BN);
+  // B box: 128 rows per load (fused epilogue: gate and up separately; CTA
+  // pairs: each CTA its half), else the whole 256-row tile
+  rc = make_tmap_b(&tb, b, E, n, k, (epi == kEpiSiluQuant || pairs) ? 128 : BN);
   if (rc) return rc;
   CUtensorMap to = ta;  // the raw int32 output is written without a tensor map
   if (epi == kEpiSiluQuant) {
@@ -900,28 +1096,28 @@ int launch_gemm(int mode, int out_dtype, bool has_bias, const int8_t* a, const i
   p.k_pad = p.kt_total * BK - p.K;
   p.n_tiles = epi == kEpiSiluQuant ? (p.n_act + 127) / 128 : static_cast<int>((n + BN - 1) / BN);
   const int64_t upper_tiles = ((sum_m + BM - 1) / BM + E) * p.n_tiles;
-  const int grid = static_cast<int>(std::min<int64_t>(num_sms(current_device()), upper_tiles));
+  const int64_t grid = upper_tiles;  // launches cap it at the resident CTAs (pairs)
   if (epi == kEpiSiluQuant) {
     if (out_dtype == I8MOE_BF16)
-      return has_bias ? launch_t<kHybrid, true, __nv_bfloat16, kEpiSiluQuant>(ta, tb, to, p, grid, st)
-                      : launch_t<kHybrid, false, __nv_bfloat16, kEpiSiluQuant>(ta, tb, to, p, grid, st);
-    return has_bias ? launch_t<kHybrid, true, __half, kEpiSiluQuant>(ta, tb, to, p, grid, st)
-                    : launch_t<kHybrid, false, __half, kEpiSiluQuant>(ta, tb, to, p, grid, st);
+      return has_bias ? launch_t<kHybrid, true, __nv_bfloat16, kEpiSiluQuant>(ta, tb, to, p, grid, pairs, st)
+                      : launch_t<kHybrid, false, __nv_bfloat16, kEpiSiluQuant>(ta, tb, to, p, grid, pairs, st);
+    return has_bias ? launch_t<kHybrid, true, __half, kEpiSiluQuant>(ta, tb, to, p, grid, pairs, st)
+                    : launch_t<kHybrid, false, __half, kEpiSiluQuant>(ta, tb, to, p, grid, pairs, st);
   }
   if (out_dtype == I8MOE_S32) {
     I8_REQUIRE(!has_bias, "the raw int32 accumulator output takes no bias");
-    return mode == kHybrid ? launch_t<kHybrid, false, int32_t>(ta, tb, to, p, grid, st)
-                           : launch_t<kPerTensor, false, int32_t>(ta, tb, to, p, grid, st);
+    return mode == kHybrid ? launch_t<kHybrid, false, int32_t>(ta, tb, to, p, grid, pairs, st)
+                           : launch_t<kPerTensor, false, int32_t>(ta, tb, to, p, grid, pairs, st);
   }
   if (mode == kHybrid) {
     if (out_dtype == I8MOE_BF16)
-      return has_bias ? launch_t<kHybrid, true, __nv_bfloat16>(ta, tb, to, p, grid, st)
-                      : launch_t<kHybrid, false, __nv_bfloat16>(ta, tb, to, p, grid, st);
-    return has_bias ? launch_t<kHybrid, true, __half>(ta, tb, to, p, grid, st)
-                    : launch_t<kHybrid, false, __half>(ta, tb, to, p, grid, st);
+      return has_bias ? launch_t<kHybrid, true, __nv_bfloat16>(ta, tb, to, p, grid, pairs, st)
+                      : launch_t<kHybrid, false, __nv_bfloat16>(ta, tb, to, p, grid, pairs, st);
+    return has_bias ? launch_t<kHybrid, true, __half>(ta, tb, to, p, grid, pairs, st)
+                    : launch_t<kHybrid, false, __half>(ta, tb, to, p, grid, pairs, st);
   }
-  if (out_dtype == I8MOE_BF16) return launch_t<kPerTensor, false, __nv_bfloat16>(ta, tb, to, p, grid, st);
-  return launch_t<kPerTensor, false, __half>(ta, tb, to, p, grid, st);
+  if (out_dtype == I8MOE_BF16) return launch_t<kPerTensor, false, __nv_bfloat16>(ta, tb, to, p, grid, pairs, st);
+  return launch_t<kPerTensor, false, __half>(ta, tb, to, p, grid, pairs, st);
 }
 
 }  // namespace
@@ -1035,6 +1231,13 @@ int i8moe_int8_grouped_mm(const int8_t* a, const int8_t* b, void* out, int out_d
   p.tile_m = BM;
   return launch_gemm(kPerTensor, out_dtype, false, a, b, p, n_expert, sum_m, n, k,
                      static_cast<cudaStream_t>(stream));
+}
+
+// Selects the CTA-pair GEMM variant: -1 by problem shape (default), 0 never,
+// 1 always.  Returns the previous setting.
+int i8moe_gemm_set_cta_pairs(int mode) {
+  I8_REQUIRE(mode >= -1 && mode <= 1, "cta pairs: mode must be -1, 0 or 1");
+  return __atomic_exchange_n(&g_cta_pairs, mode, __ATOMIC_RELAXED);
 }
 
 }  // extern "C"

@@ -44,6 +44,12 @@ def test_calls_that_need_no_gpu():
     assert lib.i8moe_route_workspace_size(65536, 256) == 32 * 512 * 4
     assert lib.i8moe_route_workspace_size(1, 8) == 1 * 16 * 4
     assert lib.i8moe_route_workspace_size(10, 0) == 0
+    # GEMM variant switch: returns the previous mode, rejects other values
+    prev = lib.i8moe_gemm_set_cta_pairs(1)
+    assert prev in (-1, 0, 1)
+    assert lib.i8moe_gemm_set_cta_pairs(0) == 1
+    assert lib.i8moe_gemm_set_cta_pairs(2) == -1 and "cta pairs" in _lib.last_error()
+    assert lib.i8moe_gemm_set_cta_pairs(prev) == 0
 
 
 def test_argument_errors_before_any_cuda_call():

@@ -37,6 +37,18 @@ def m():
     assert _lib.device_error(0) == 0, "a kernel reported a device-side error"
 
 
+@pytest.fixture
+def cta_pairs(request, m):
+    """Force the grouped-GEMM variant for one test: 0 = one CTA per 128-row
+    tile, 1 = CTA pairs (cta_group::2, 256-row pair tiles)."""
+    prev = m._lib.set_cta_pairs(request.param)
+    yield request.param
+    m._lib.set_cta_pairs(prev)
+
+
+PAIRS = pytest.mark.parametrize("cta_pairs", [0, 1], indirect=True, ids=["cta1", "cta2"])
+
+
 def npf(t: torch.Tensor) -> np.ndarray:
     t = t.detach().cpu()
     if t.is_floating_point():
@@ -221,8 +233,9 @@ GEMM_CASES = [
 ]
 
 
+@PAIRS
 @pytest.mark.parametrize("case", GEMM_CASES, ids=lambda c: f"s{c['seed']}")
-def test_hybrid_gemm_bit_exact(m, case):
+def test_hybrid_gemm_bit_exact(m, case, cta_pairs):
     c = _gemm_case(**case)
     d = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in c.items()}
     fn = (m.ops.cutlass_int8_blockwise_hybrid_grouped if c["tm"] == 128
@@ -246,7 +259,8 @@ def test_hybrid_gemm_bit_exact(m, case):
         np.testing.assert_array_equal(npf(out), exp)
 
 
-def test_hybrid_gemm_bias(m):
+@PAIRS
+def test_hybrid_gemm_bias(m, cta_pairs):
     c = _gemm_case(seed=7, counts=[100, 0, 60], N=192, K=256)
     d = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in c.items()}
     g = torch.Generator().manual_seed(9)
@@ -382,9 +396,10 @@ FWD_GOLDEN = [("fwd_tiny", "tiny", True, True, None), ("fwd_tiny_unfused", "tiny
               ("fwd_tiny_ep1of2", "tiny", True, True, (1, 2))]
 
 
+@PAIRS
 @pytest.mark.parametrize("fuse_w13", [False, True], ids=["w13-store", "w13-silu-epilogue"])
 @pytest.mark.parametrize("gname,cname,fp,fs,ep", FWD_GOLDEN, ids=[f[0] for f in FWD_GOLDEN])
-def test_forward_against_reference_golden(m, gname, cname, fp, fs, ep, fuse_w13):
+def test_forward_against_reference_golden(m, gname, cname, fp, fs, ep, fuse_w13, cta_pairs):
     g = dict(np.load(GOLDEN / f"{gname}.npz"))
     cfg, inp = inputs(cname)
     emap, sl = None, None
@@ -473,8 +488,9 @@ def test_forward_default_config_stagewise(m):
 FUSED_W13_CASES = ["tiny", "ragged", "tm128", "mid", "large_small", "default"]
 
 
+@PAIRS
 @pytest.mark.parametrize("cname", FUSED_W13_CASES)
-def test_fused_w13_epilogue_matches_gemm_then_silu_quant(m, cname):
+def test_fused_w13_epilogue_matches_gemm_then_silu_quant(m, cname, cta_pairs):
     """The w13 GEMM with SiLU*up + requant in its epilogue produces the same
     INT8 activations, block scales, Q/F factors (and hence mm2 and output)
     bit for bit as the w13 GEMM followed by the fused SiLU-quant kernel."""
@@ -499,6 +515,37 @@ def test_fused_w13_epilogue_matches_gemm_then_silu_quant(m, cname):
     assert torch.equal(ta["a2_F"][:nrows], tb["a2_F"][:nrows])
     # bit patterns: fp16 outputs of the large config overflow to inf/NaN
     bits = {torch.float16: torch.int16, torch.bfloat16: torch.int16, torch.float32: torch.int32}
+    assert torch.equal(ta["mm2"][:v].view(bits[out_a.dtype]), tb["mm2"][:v].view(bits[out_a.dtype]))
+    assert torch.equal(out_a.view(bits[out_a.dtype]), out_b.view(bits[out_a.dtype]))
+    assert m._lib.device_error(0) == 0
+
+
+@pytest.mark.parametrize("cname", ["default", "skewed", "mid", "large_small"])
+def test_cta_pairs_match_single_cta(m, cname):
+    """The CTA-pair GEMMs (cta_group::2) give the single-CTA results bit for
+    bit: a2q, its Q/F, mm2 and the output of the whole forward."""
+    if cname == "large_small":
+        wl = load_workloads()
+        from dataclasses import replace
+        cfg = replace(wl.CONFIGS["large"], T=512)
+        inp = wl.make_inputs(cfg)
+    else:
+        cfg, inp = inputs(cname)
+    prev = m._lib.set_cta_pairs(0)
+    try:
+        ta, tb = {}, {}
+        out_a = run_forward(m, cfg, inp, True, True, trace=ta).clone()
+        m._lib.set_cta_pairs(1)
+        out_b = run_forward(m, cfg, inp, True, True, trace=tb).clone()
+    finally:
+        m._lib.set_cta_pairs(prev)
+    v = int(ta["eft"][-1])
+    counts = npf(ta["eft"])[1:] - npf(ta["eft"])[:-1]
+    nrows = int(((counts + ta["tile_m"] - 1) // ta["tile_m"]).sum())
+    assert torch.equal(ta["a2q"][:v], tb["a2q"][:v])
+    assert torch.equal(ta["a2_Q"][:nrows], tb["a2_Q"][:nrows])
+    assert torch.equal(ta["a2_F"][:nrows], tb["a2_F"][:nrows])
+    bits = {torch.float16: torch.int16, torch.bfloat16: torch.int16}
     assert torch.equal(ta["mm2"][:v].view(bits[out_a.dtype]), tb["mm2"][:v].view(bits[out_a.dtype]))
     assert torch.equal(out_a.view(bits[out_a.dtype]), out_b.view(bits[out_a.dtype]))
     assert m._lib.device_error(0) == 0
