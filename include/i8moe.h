@@ -323,6 +323,61 @@ int i8moe_ep_combine(const void* back, int dtype, const int32_t* pos, int64_t n_
                      int64_t n_rank, const int64_t* counts, int64_t n_hidden, void* out,
                      i8moe_stream_t stream);
 
+/* ----------------------------------------- expert parallelism, peer memory */
+/* No reference counterpart: the same dispatch / combine without NCCL and
+ * without any host synchronisation, over NVLink peer memory.  Each rank
+ * allocates one region (i8moe_ep_ipc_alloc), exchanges the 64-byte IPC
+ * handles with the other ranks (any host channel) and maps theirs
+ * (i8moe_ep_ipc_open).  A step on every rank, in order on one stream:
+ *   i8moe_ep_plan          (pos, token_list, counts: device arrays)
+ *   i8moe_ep_p2p_dispatch  rows, ids and weights into the destinations'
+ *                          receive buffers; waits (bounded) for the peers'
+ *                          segment lengths
+ *   i8moe_ep_p2p_wait      until every source's rows have arrived
+ *   the local forward over the `capacity` receive rows (rows past the
+ *                          received ones carry `pad_expert`, an expert of
+ *                          another rank, so the local routing skips them),
+ *                          writing its [capacity, n_hidden] output into the
+ *                          region's output buffer of the step's parity
+ *   i8moe_ep_p2p_ready     announces that output to the peers
+ *   i8moe_ep_p2p_combine   sums each token's partial rows from the peers'
+ *                          output buffers in rank order (fp32) into out.
+ * `par` is the step number modulo 2 (the same on every rank).  Waits give
+ * up after 2 s and set a bit in i8moe_device_error.  No multicast objects
+ * are created. */
+#define I8MOE_IPC_HANDLE_BYTES 64
+
+typedef struct {
+  int64_t off_rows, off_ids, off_w, off_out, out_bytes, off_inbox, off_flags, off_epoch;
+  int64_t bytes; /* region size */
+} i8moe_ep_p2p_layout;
+
+typedef struct {
+  void* bases[32];        /* every rank's region, mapped in this process */
+  int64_t n_rank, rank;
+  int64_t n_token;        /* tokens of this rank */
+  int64_t capacity;       /* receive rows: n_rank x max tokens per rank */
+  int64_t topk, n_hidden, elem_bytes; /* elem_bytes: 2 (bf16 / fp16) */
+  int64_t pad_expert;     /* a global expert id owned by another rank */
+  i8moe_ep_p2p_layout layout;
+} i8moe_ep_p2p;
+
+int i8moe_ep_p2p_region_bytes(int64_t n_rank, int64_t capacity, int64_t topk, int64_t n_hidden,
+                              int64_t elem_bytes, i8moe_ep_p2p_layout* layout);
+/* cudaMalloc'd (zeroed) region and its IPC handle (I8MOE_IPC_HANDLE_BYTES) */
+int i8moe_ep_ipc_alloc(int64_t bytes, void** ptr, uint8_t* handle);
+int i8moe_ep_ipc_open(const uint8_t* handle, void** ptr);
+int i8moe_ep_ipc_close(void* ptr);
+int i8moe_ep_ipc_free(void* ptr);
+int i8moe_ep_p2p_dispatch(const i8moe_ep_p2p* x, int par, const void* hidden,
+                          const int32_t* topk_ids, const float* topk_weights,
+                          const int32_t* token_list, const int32_t* counts,
+                          i8moe_stream_t stream);
+int i8moe_ep_p2p_wait(const i8moe_ep_p2p* x, int par, i8moe_stream_t stream);
+int i8moe_ep_p2p_ready(const i8moe_ep_p2p* x, int par, i8moe_stream_t stream);
+int i8moe_ep_p2p_combine(const i8moe_ep_p2p* x, int par, int dtype, const int32_t* pos, void* out,
+                         i8moe_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

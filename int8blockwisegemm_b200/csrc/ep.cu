@@ -14,11 +14,59 @@
 // These replace host-driven torch glue (nonzero, index_select, index_add_)
 // and keep the exchange to a single host synchronisation: the segment
 // lengths that size the NCCL transfers.
+//
+// The peer-memory exchange (ep_p2p_*) needs no NCCL call and no host
+// synchronisation at all.  Every rank owns one device region, mapped into
+// every other rank's process through CUDA IPC (plain NVLink peer access):
+//
+//   rows   [C, K]     receive rows         (written by the sources)
+//   ids    [C, k]     their top-k ids       (written by the sources)
+//   w      [C, k]     their top-k weights   (written by the sources)
+//   out    [2][C, K]  local forward output, by step parity (read by sources)
+//   inbox  [2][P][P]  every source's segment lengths, by step parity
+//   flags  [3][P]     epochs: lengths posted, rows posted, output ready
+//   epoch, counter    this rank's step number and a CTA completion counter
+//
+// with C = P x (tokens per rank) rows of capacity.  A step is
+//   dispatch: post the P lengths to every peer, wait (bounded) for all of
+//             theirs, then store every row straight into its destination's
+//             receive buffer at its final offset (sources in rank order,
+//             tokens in order: the same row order as the NCCL path); the
+//             last CTA to finish raises this rank's "rows posted" flag at
+//             every peer;
+//   wait:     until every source has posted its rows; rows past the
+//             received ones get a non-local expert id (the local routing
+//             skips them);
+//   (the unchanged single-GPU forward over the C receive rows)
+//   ready:    raise this rank's "output ready" flag at every peer;
+//   combine:  wait for every destination's output, then sum this rank's
+//             tokens' partial rows, read from the peers' memory, in rank
+//             order in fp32.
+// Flags carry the step number and waits test flag >= step, so a peer that
+// runs a step ahead never blocks one behind; a peer can never run two
+// steps ahead (a step's dispatch needs every peer's previous output to
+// have been combined).  Every wait gives up after kP2PTimeoutNs with an
+// error bit (i8moe_device_error) instead of hanging.
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 
 namespace i8moe {
+
+static __device__ unsigned g_err_ep;
+
+int read_ep_error(uint32_t* w, int clear) {
+  unsigned v = 0;
+  I8_CUDA(cudaMemcpyFromSymbol(&v, g_err_ep, sizeof(v)));
+  if (clear) {
+    unsigned z = 0;
+    I8_CUDA(cudaMemcpyToSymbol(g_err_ep, &z, sizeof(z)));
+  }
+  *w = v;
+  return I8MOE_OK;
+}
+
 namespace {
 
 constexpr int kPlanThreads = 1024;
@@ -131,6 +179,218 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const T* __restrict__ b
   }
 }
 
+// ---------------------------------------------------------------------------
+// peer-memory exchange
+// ---------------------------------------------------------------------------
+constexpr uint64_t kP2PTimeoutNs = 2000000000ull;  // 2 s
+constexpr unsigned kErrPeerTimeout = 1u << 6;
+
+struct P2PArgs {
+  uint8_t* base[kMaxRanks];  // every rank's region as mapped in this process
+  int P, rank;
+  int T;                     // tokens of this rank
+  int C;                     // receive capacity (rows)
+  int k, K, esize;           // top-k, hidden, bytes per hidden element
+  int pad_id;                // a global expert id no local expert has
+  int par;                   // step parity
+  int64_t off_rows, off_ids, off_w, off_out, out_bytes, off_inbox, off_flags, off_epoch;
+};
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t* flag_ptr(const P2PArgs& a, int owner, int kind, int src) {
+  return reinterpret_cast<uint64_t*>(a.base[owner] + a.off_flags) + kind * a.P + src;
+}
+__device__ __forceinline__ int32_t* inbox_ptr(const P2PArgs& a, int owner) {
+  return reinterpret_cast<int32_t*>(a.base[owner] + a.off_inbox) + a.par * a.P * a.P;
+}
+__device__ __forceinline__ uint64_t my_epoch(const P2PArgs& a) {
+  return *reinterpret_cast<volatile uint64_t*>(a.base[a.rank] + a.off_epoch);
+}
+// one thread: until this rank's flags `kind` from every rank reach `ep`
+__device__ bool wait_flags(const P2PArgs& a, int kind, uint64_t ep) {
+  const uint64_t t0 = globaltimer();
+  for (int s = 0; s < a.P; ++s) {
+    const uint64_t* f = flag_ptr(a, a.rank, kind, s);
+    while (ld_acquire_sys(f) < ep) {
+      if (globaltimer() - t0 > kP2PTimeoutNs) {
+        atomicOr(&g_err_ep, kErrPeerTimeout);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+enum { kFlagCounts = 0, kFlagRows = 1, kFlagOut = 2 };
+
+__global__ void ep_p2p_begin(P2PArgs a) {
+  uint64_t* e = reinterpret_cast<uint64_t*>(a.base[a.rank] + a.off_epoch);
+  *e = *e + 1;
+}
+
+// Offsets of this rank's segment in every destination's receive buffer:
+// off_to[d] = sum over sources s < rank of count[s][d] (shared memory).
+__device__ void p2p_offsets(const P2PArgs& a, int* off_to) {
+  const int32_t* inbox = inbox_ptr(a, a.rank);
+  if (threadIdx.x < a.P) {
+    const int d = threadIdx.x;
+    int o = 0;
+    for (int s = 0; s < a.rank; ++s) o += __ldcg(inbox + s * a.P + d);  // written by peers
+    off_to[d] = o;
+  }
+}
+
+__global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(P2PArgs a, const uint4* __restrict__ hidden,
+                                                              const int32_t* __restrict__ ids,
+                                                              const float* __restrict__ w,
+                                                              const int32_t* __restrict__ list,
+                                                              const int32_t* __restrict__ counts,
+                                                              unsigned* __restrict__ done_ctr) {
+  __shared__ int s_off[kMaxRanks], s_seg[kMaxRanks + 1];
+  __shared__ int s_ok;
+  const uint64_t ep = my_epoch(a);
+  if (blockIdx.x == 0 && threadIdx.x < a.P) {
+    // post this rank's segment lengths to destination d, then the flag
+    const int d = threadIdx.x;
+    int32_t* dst = inbox_ptr(a, d) + a.rank * a.P;
+    for (int j = 0; j < a.P; ++j) dst[j] = __ldg(counts + j);
+    __threadfence_system();
+    st_release_sys(flag_ptr(a, d, kFlagCounts, a.rank), ep);
+  }
+  if (threadIdx.x == 0) s_ok = wait_flags(a, kFlagCounts, ep) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  p2p_offsets(a, s_off);
+  if (threadIdx.x == 0) {
+    int o = 0;
+    for (int d = 0; d < a.P; ++d) {
+      s_seg[d] = o;
+      o += __ldg(counts + d);
+    }
+    s_seg[a.P] = o;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t chunks = static_cast<int64_t>(a.K) * a.esize / 16;
+  const int64_t n_rows = s_seg[a.P];
+  const int wpb = blockDim.x / 32;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); g < n_rows;
+       g += static_cast<int64_t>(gridDim.x) * wpb) {
+    int d = 0;
+    while (d + 1 < a.P && s_seg[d + 1] <= g) ++d;
+    const int p = static_cast<int>(g - s_seg[d]);
+    const int t = __ldg(list + static_cast<int64_t>(d) * a.T + p);
+    const int64_t row = s_off[d] + p;  // in d's receive buffer
+    if (row >= a.C) {  // capacity is P x tokens per rank, so never
+      if (lane == 0) atomicOr(&g_err_ep, kErrBadIndex);
+      continue;
+    }
+    const uint4* src = hidden + static_cast<int64_t>(t) * chunks;
+    uint4* dst = reinterpret_cast<uint4*>(a.base[d] + a.off_rows) + row * chunks;
+    for (int64_t c = lane; c < chunks; c += 32) dst[c] = __ldg(src + c);
+    if (lane < a.k) {
+      reinterpret_cast<int32_t*>(a.base[d] + a.off_ids)[row * a.k + lane] =
+          __ldg(ids + static_cast<int64_t>(t) * a.k + lane);
+      reinterpret_cast<float*>(a.base[d] + a.off_w)[row * a.k + lane] =
+          __ldg(w + static_cast<int64_t>(t) * a.k + lane);
+    }
+  }
+  // the last CTA to finish raises the "rows posted" flag at every peer
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned old = atomicAdd(done_ctr, 1u);
+    if (old == gridDim.x - 1) {
+      *done_ctr = 0u;
+      __threadfence_system();
+      for (int d = 0; d < a.P; ++d) st_release_sys(flag_ptr(a, d, kFlagRows, a.rank), ep);
+    }
+  }
+}
+
+// Until every source has posted its rows; then the receive rows past the
+// received ones get a non-local expert id and weight 0.
+__global__ void __launch_bounds__(256) ep_p2p_wait_kernel(P2PArgs a) {
+  __shared__ int s_ok;
+  const uint64_t ep = my_epoch(a);
+  if (threadIdx.x == 0) s_ok = wait_flags(a, kFlagRows, ep) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  const int32_t* inbox = inbox_ptr(a, a.rank);
+  int n_recv = 0;
+  for (int s = 0; s < a.P; ++s) n_recv += __ldcg(inbox + s * a.P + a.rank);
+  n_recv = min(n_recv, a.C);
+  int32_t* rid = reinterpret_cast<int32_t*>(a.base[a.rank] + a.off_ids);
+  float* rw = reinterpret_cast<float*>(a.base[a.rank] + a.off_w);
+  const int64_t n_pad = static_cast<int64_t>(a.C - n_recv) * a.k;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_pad;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    rid[static_cast<int64_t>(n_recv) * a.k + i] = a.pad_id;
+    rw[static_cast<int64_t>(n_recv) * a.k + i] = 0.0f;
+  }
+}
+
+// This rank's local forward output (a previous kernel on the stream) is
+// complete: raise the "output ready" flag at every peer.
+__global__ void ep_p2p_ready_kernel(P2PArgs a) {
+  const uint64_t ep = my_epoch(a);
+  __threadfence_system();
+  if (threadIdx.x < a.P) st_release_sys(flag_ptr(a, threadIdx.x, kFlagOut, a.rank), ep);
+}
+
+// out[t] = dtype(sum over destinations d in rank order of d's output row
+// off_to[d] + pos[t, d]), fp32 accumulation, rows read from peer memory.
+template <typename T>
+__global__ void __launch_bounds__(256) ep_p2p_combine_kernel(P2PArgs a, const int32_t* __restrict__ pos,
+                                                             T* __restrict__ out) {
+  constexpr int EPC = 8;
+  __shared__ int s_off[kMaxRanks];
+  __shared__ int s_ok;
+  const uint64_t ep = my_epoch(a);
+  if (threadIdx.x == 0) s_ok = wait_flags(a, kFlagOut, ep) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  p2p_offsets(a, s_off);
+  __syncthreads();
+  const int chunks = a.K / EPC;
+  for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+    int64_t rows[kMaxRanks];
+    int owner[kMaxRanks];
+    int nr = 0;
+    for (int d = 0; d < a.P; ++d) {
+      const int p = __ldg(pos + static_cast<int64_t>(t) * a.P + d);
+      if (p >= 0 && s_off[d] + p < a.C) {
+        rows[nr] = s_off[d] + p;
+        owner[nr++] = d;
+      }
+    }
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+      float acc[EPC];
+#pragma unroll
+      for (int i = 0; i < EPC; ++i) acc[i] = 0.f;
+      for (int r = 0; r < nr; ++r) {
+        const T* src = reinterpret_cast<const T*>(a.base[owner[r]] + a.off_out + a.par * a.out_bytes) +
+                       rows[r] * a.K;
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + c);  // peer memory, via L2
+        const T* x = reinterpret_cast<const T*>(&v);
+#pragma unroll
+        for (int i = 0; i < EPC; ++i) acc[i] += Num<T>::to_f(x[i]);
+      }
+      uint4 o;
+      T* y = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int i = 0; i < EPC; ++i) y[i] = Num<T>::from_f(acc[i]);
+      reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * a.K)[c] = o;
+    }
+  }
+}
+
 int offsets_from(const int64_t* counts, int P, RankOffsets* ro) {
   I8_REQUIRE(P >= 1 && P <= kMaxRanks, "ep: the group must have 1..%d ranks", kMaxRanks);
   ro->off[0] = 0;
@@ -182,6 +442,157 @@ int i8moe_ep_pack(const void* hidden, int64_t row_bytes, const int32_t* topk_ids
       static_cast<int>(topk), token_list, static_cast<int>(n_token), static_cast<int>(n_rank), ro,
       static_cast<uint4*>(send_rows), send_meta);
   return check_launch("ep_pack");
+}
+
+int i8moe_ep_p2p_region_bytes(int64_t n_rank, int64_t capacity, int64_t topk, int64_t n_hidden,
+                              int64_t elem_bytes, i8moe_ep_p2p_layout* layout) {
+  I8_REQUIRE(n_rank >= 1 && n_rank <= kMaxRanks, "ep p2p: the group must have 1..%d ranks", kMaxRanks);
+  I8_REQUIRE(capacity >= 1 && topk >= 1 && topk <= 32 && n_hidden >= 8 && elem_bytes == 2 &&
+                 (n_hidden * elem_bytes) % 16 == 0,
+             "ep p2p: bad shape");
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  i8moe_ep_p2p_layout l{};
+  int64_t o = 0;
+  l.off_rows = o;  o = up(o + capacity * n_hidden * elem_bytes);
+  l.off_ids = o;   o = up(o + capacity * topk * 4);
+  l.off_w = o;     o = up(o + capacity * topk * 4);
+  l.off_out = o;   l.out_bytes = up(capacity * n_hidden * elem_bytes);
+  o = up(o + 2 * l.out_bytes);
+  l.off_inbox = o; o = up(o + 2 * n_rank * n_rank * 4);
+  l.off_flags = o; o = up(o + 3 * n_rank * 8);
+  l.off_epoch = o; o = up(o + 16);  // epoch (8 B), CTA completion counter (4 B)
+  l.bytes = o;
+  *layout = l;
+  return I8MOE_OK;
+}
+
+int i8moe_ep_ipc_alloc(int64_t bytes, void** ptr, uint8_t* handle) {
+  I8_REQUIRE(bytes > 0 && ptr != nullptr && handle != nullptr, "ep ipc: bad arguments");
+  void* p = nullptr;
+  I8_CUDA(cudaMalloc(&p, static_cast<size_t>(bytes)));
+  cudaError_t e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return set_error(I8MOE_ERR_CUDA, std::string("ep ipc alloc: ") + cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == I8MOE_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return I8MOE_OK;
+}
+
+int i8moe_ep_ipc_open(const uint8_t* handle, void** ptr) {
+  I8_REQUIRE(handle != nullptr && ptr != nullptr, "ep ipc: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  I8_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *ptr = p;
+  return I8MOE_OK;
+}
+
+int i8moe_ep_ipc_close(void* ptr) {
+  I8_CUDA(cudaIpcCloseMemHandle(ptr));
+  return I8MOE_OK;
+}
+
+int i8moe_ep_ipc_free(void* ptr) {
+  I8_CUDA(cudaFree(ptr));
+  return I8MOE_OK;
+}
+
+}  // extern "C"
+
+namespace {
+int p2p_args(const i8moe_ep_p2p* x, int par, P2PArgs* a) {
+  I8_REQUIRE(x != nullptr && x->n_rank >= 1 && x->n_rank <= kMaxRanks && x->rank >= 0 &&
+                 x->rank < x->n_rank,
+             "ep p2p: bad group");
+  I8_REQUIRE(x->capacity >= 1 && x->topk >= 1 && x->topk <= 32 && x->elem_bytes == 2,
+             "ep p2p: bad shape");
+  *a = P2PArgs{};
+  for (int d = 0; d < x->n_rank; ++d) {
+    I8_REQUIRE(x->bases[d] != nullptr, "ep p2p: region of rank %d is not mapped", d);
+    a->base[d] = static_cast<uint8_t*>(x->bases[d]);
+  }
+  a->P = static_cast<int>(x->n_rank);
+  a->rank = static_cast<int>(x->rank);
+  a->T = static_cast<int>(x->n_token);
+  a->C = static_cast<int>(x->capacity);
+  a->k = static_cast<int>(x->topk);
+  a->K = static_cast<int>(x->n_hidden);
+  a->esize = static_cast<int>(x->elem_bytes);
+  a->pad_id = static_cast<int>(x->pad_expert);
+  a->par = par & 1;
+  a->off_rows = x->layout.off_rows;
+  a->off_ids = x->layout.off_ids;
+  a->off_w = x->layout.off_w;
+  a->off_out = x->layout.off_out;
+  a->out_bytes = x->layout.out_bytes;
+  a->off_inbox = x->layout.off_inbox;
+  a->off_flags = x->layout.off_flags;
+  a->off_epoch = x->layout.off_epoch;
+  return I8MOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int i8moe_ep_p2p_dispatch(const i8moe_ep_p2p* x, int par, const void* hidden,
+                          const int32_t* topk_ids, const float* topk_weights,
+                          const int32_t* token_list, const int32_t* counts,
+                          i8moe_stream_t stream) {
+  P2PArgs a;
+  int rc = p2p_args(x, par, &a);
+  if (rc) return rc;
+  I8_REQUIRE(reinterpret_cast<uintptr_t>(hidden) % 16 == 0, "ep p2p: hidden must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ep_p2p_begin<<<1, 1, 0, st>>>(a);
+  rc = check_launch("ep_p2p_begin");
+  if (rc) return rc;
+  unsigned* ctr = reinterpret_cast<unsigned*>(a.base[a.rank] + a.off_epoch + 8);
+  const unsigned grid = static_cast<unsigned>(2 * num_sms(current_device()));
+  ep_p2p_dispatch_kernel<<<grid, 256, 0, st>>>(a, static_cast<const uint4*>(hidden), topk_ids,
+                                               topk_weights, token_list, counts, ctr);
+  return check_launch("ep_p2p_dispatch");
+}
+
+int i8moe_ep_p2p_wait(const i8moe_ep_p2p* x, int par, i8moe_stream_t stream) {
+  P2PArgs a;
+  int rc = p2p_args(x, par, &a);
+  if (rc) return rc;
+  ep_p2p_wait_kernel<<<static_cast<unsigned>(num_sms(current_device())), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("ep_p2p_wait");
+}
+
+int i8moe_ep_p2p_ready(const i8moe_ep_p2p* x, int par, i8moe_stream_t stream) {
+  P2PArgs a;
+  int rc = p2p_args(x, par, &a);
+  if (rc) return rc;
+  ep_p2p_ready_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("ep_p2p_ready");
+}
+
+int i8moe_ep_p2p_combine(const i8moe_ep_p2p* x, int par, int dtype, const int32_t* pos, void* out,
+                         i8moe_stream_t stream) {
+  P2PArgs a;
+  int rc = p2p_args(x, par, &a);
+  if (rc) return rc;
+  I8_REQUIRE(dtype == I8MOE_BF16 || dtype == I8MOE_FP16, "ep p2p combine: bfloat16 or float16 rows");
+  I8_REQUIRE(a.K % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0,
+             "ep p2p combine: 16-byte rows");
+  if (a.T == 0) return I8MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(a.T, 4 * num_sms(current_device())));
+  if (dtype == I8MOE_BF16)
+    ep_p2p_combine_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a, pos, static_cast<__nv_bfloat16*>(out));
+  else
+    ep_p2p_combine_kernel<__half><<<grid, 256, 0, st>>>(a, pos, static_cast<__half*>(out));
+  return check_launch("ep_p2p_combine");
 }
 
 int i8moe_ep_combine(const void* back, int dtype, const int32_t* pos, int64_t n_token,

@@ -193,6 +193,136 @@ class ExpertParallel:
         return self.combine(d, partial, out)
 
 
+class _Layout(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int64) for n in ("off_rows", "off_ids", "off_w", "off_out", "out_bytes",
+                                              "off_inbox", "off_flags", "off_epoch", "bytes")]
+
+
+class _P2PDesc(ctypes.Structure):
+    """``i8moe_ep_p2p`` of include/i8moe.h."""
+    _fields_ = [("bases", ctypes.c_void_p * 32), ("n_rank", ctypes.c_int64), ("rank", ctypes.c_int64),
+                ("n_token", ctypes.c_int64), ("capacity", ctypes.c_int64), ("topk", ctypes.c_int64),
+                ("n_hidden", ctypes.c_int64), ("elem_bytes", ctypes.c_int64),
+                ("pad_expert", ctypes.c_int64), ("layout", _Layout)]
+
+
+class _DeviceArray:
+    """A borrowed device buffer seen through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape),
+                                         "typestr": typestr, "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Expert-parallel dispatch / combine over NVLink peer memory: no NCCL
+    call and no host synchronisation in a step (csrc/ep.cu, ``ep_p2p_*``).
+
+    Every rank allocates one region (receive rows, ids and weights for
+    ``capacity = world * max_tokens`` rows, two output buffers, the
+    segment-length inbox and the step flags) and maps the other ranks'
+    regions through CUDA IPC handles exchanged once over the process group.
+    A step runs ep_plan, the dispatch (rows stored straight into the
+    destinations' receive buffers), a wait for every source's rows, the
+    local forward over the ``capacity`` receive rows into this step's
+    output buffer, the "output ready" signal and the combine (partial rows
+    read from the peers' output buffers, summed in rank order).  Every shape
+    is static, so whole steps can be captured in CUDA graphs."""
+
+    def __init__(self, ep: ExpertParallel, max_tokens: int, n_hidden: int, topk: int,
+                 dtype: torch.dtype, device):
+        from ._lib import call
+        assert dtype in (torch.bfloat16, torch.float16) and ep.world >= 2
+        self.ep, self.device, self.dtype = ep, torch.device(device), dtype
+        P, r = ep.world, ep.rank
+        self.P, self.k, self.K, self.T = P, topk, n_hidden, max_tokens
+        self.C = P * max_tokens
+        lay = _Layout()
+        call("i8moe_ep_p2p_region_bytes", P, self.C, topk, n_hidden, 2, ctypes.addressof(lay))
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_uint8 * 64)()
+        with torch.cuda.device(self.device):
+            call("i8moe_ep_ipc_alloc", lay.bytes, ctypes.addressof(ptr), ctypes.addressof(handle))
+        self._own = ptr.value
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        every = torch.empty(P * 64, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(every, mine, group=ep.group)
+        every = every.view(P, 64).cpu()
+        self._opened = []
+        desc = _P2PDesc()
+        for d in range(P):
+            if d == r:
+                desc.bases[d] = self._own
+                continue
+            h = (ctypes.c_uint8 * 64)(*every[d].tolist())
+            p = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                call("i8moe_ep_ipc_open", ctypes.addressof(h), ctypes.addressof(p))
+            self._opened.append(p.value)
+            desc.bases[d] = p.value
+        desc.n_rank, desc.rank, desc.n_token, desc.capacity = P, r, max_tokens, self.C
+        desc.topk, desc.n_hidden, desc.elem_bytes = topk, n_hidden, 2
+        # an expert of the next rank: the local routing skips padding rows
+        desc.pad_expert = ((r + 1) % P) * ep.n_local
+        desc.layout = lay
+        self._desc = desc
+        base, C, k, K = self._own, self.C, topk, n_hidden
+        as_t = lambda off, shape, ts: torch.as_tensor(_DeviceArray(base + off, shape, ts),
+                                                      device=self.device)
+        self.recv_rows = as_t(lay.off_rows, (C, K), "<i2").view(dtype)
+        self.recv_ids = as_t(lay.off_ids, (C, k), "<i4")
+        self.recv_w = as_t(lay.off_w, (C, k), "<f4")
+        self.out_buf = [as_t(lay.off_out + i * lay.out_bytes, (C, K), "<i2").view(dtype)
+                        for i in range(2)]
+        self.pos = torch.empty(max_tokens, P, dtype=torch.int32, device=self.device)
+        self.lst = torch.empty(P, max_tokens, dtype=torch.int32, device=self.device)
+        self.counts = torch.empty(P, dtype=torch.int32, device=self.device)
+        self.step = 0
+        dist.barrier(group=ep.group)  # every region is mapped before any rank writes into one
+
+    def forward(self, hidden, topk_ids, topk_weights, local_forward, out=None):
+        """One expert-parallel step; ``local_forward(rows, ids, weights, out)``
+        runs the local experts over the ``capacity`` receive rows into out."""
+        from ._lib import BF16, FP16, call
+        T, k = topk_ids.shape
+        assert T <= self.T and k == self.k and hidden.shape[1] == self.K
+        assert hidden.dtype == self.dtype and hidden.is_contiguous()
+        par = self.step & 1
+        self.step += 1
+        self._desc.n_token = T
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        ids = topk_ids.to(torch.int32).contiguous()
+        wts = topk_weights.to(torch.float32).contiguous()
+        if out is None:
+            out = torch.empty(T, self.K, dtype=self.dtype, device=self.device)
+        d = ctypes.addressof(self._desc)
+        with torch.cuda.device(self.device):
+            call("i8moe_ep_plan", ids.data_ptr(), T, k, self.ep.n_local, self.P,
+                 self.pos.data_ptr(), self.lst.data_ptr(), self.counts.data_ptr(), st)
+            call("i8moe_ep_p2p_dispatch", d, par, hidden.data_ptr(), ids.data_ptr(),
+                 wts.data_ptr(), self.lst.data_ptr(), self.counts.data_ptr(), st)
+            call("i8moe_ep_p2p_wait", d, par, st)
+        local_forward(self.recv_rows, self.recv_ids, self.recv_w, self.out_buf[par])
+        dt = {torch.bfloat16: BF16, torch.float16: FP16}[self.dtype]
+        with torch.cuda.device(self.device):
+            call("i8moe_ep_p2p_ready", d, par, st)
+            call("i8moe_ep_p2p_combine", d, par, dt, self.pos.data_ptr(), out.data_ptr(), st)
+        return out
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (collective)."""
+        from ._lib import call
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.ep.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                call("i8moe_ep_ipc_close", p)
+            dist.barrier(group=self.ep.group)
+            call("i8moe_ep_ipc_free", self._own)
+        self._own = None
+
+
 def global_tile_m(n_token_global: int, topk: int, num_experts: int) -> int:
     """tile_m of the single-GPU run (cutlass_runner.py:43-50 on the global
     rows per expert), which keeps the EP quant tiles identical to it."""
@@ -225,12 +355,13 @@ class EPMoE:
                         torch.empty(need2, dtype=dtype, device=device))
         return self._ws[0][:need13].view(rows, -1), self._ws[1][:need2].view(rows, -1)
 
-    def local_forward(self, hidden, topk_ids, topk_weights, trace: dict | None = None):
+    def local_forward(self, hidden, topk_ids, topk_weights, trace: dict | None = None, out=None):
         from .activation import MoEActivation
         from .cutlass_runner import _run_cutlass_int8_hybrid_grouped_moe
         T, k = topk_ids.shape
         K, N = hidden.shape[1], self.w2.shape[2]
-        out = torch.empty(T, K, dtype=hidden.dtype, device=hidden.device)
+        if out is None:
+            out = torch.empty(T, K, dtype=hidden.dtype, device=hidden.device)
         if T == 0:
             return out
         ws13, ws2 = self._workspaces(T * k, K, N, hidden.dtype, hidden.device)
@@ -240,7 +371,17 @@ class EPMoE:
             ws13, ws2, self.qbs, self.sg, self.q_max, _trace=trace, _tile_m=self.tile_m)
         return out
 
+    def enable_peer_exchange(self, max_tokens: int, n_hidden: int, topk: int, dtype):
+        """Use the NVLink peer-memory exchange (no NCCL, no host
+        synchronisation) for steps of up to ``max_tokens`` tokens per rank."""
+        self.p2p = PeerExchange(self.ep, max_tokens, n_hidden, topk, dtype, self.w1.device)
+        return self.p2p
+
     def forward(self, hidden, topk_ids, topk_weights, out=None, trace: dict | None = None):
+        p2p = getattr(self, "p2p", None)
+        if p2p is not None and hidden.is_cuda:
+            return p2p.forward(hidden, topk_ids, topk_weights,
+                               lambda h, i, w, o: self.local_forward(h, i, w, trace, out=o), out)
         return self.ep.forward(
             hidden, topk_ids, topk_weights,
             lambda h, i, w: self.local_forward(h, i, w, trace), out)

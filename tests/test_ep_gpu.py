@@ -1,9 +1,11 @@
-"""Expert parallelism on two GPUs over NCCL.  Each rank runs the EP forward
-(dispatch all-to-all -> sm_100a forward of its local experts -> combine) and,
-on its own GPU, the single-GPU forward of all tokens; per local expert the
-INT8 activations, mm1, a2q and mm2 rows must be bit-identical, and the
-combined output within the reference tolerance (max-abs-rel 1e-2).  Needs
-two GPUs; skipped otherwise."""
+"""Expert parallelism on two GPUs, over NCCL and over NVLink peer memory.
+Each rank runs the EP forward (dispatch -> sm_100a forward of its local
+experts -> combine) and, on its own GPU, the single-GPU forward of all
+tokens; per local expert the INT8 activations, mm1, a2q and mm2 rows must be
+bit-identical, and the combined output within the reference tolerance
+(max-abs-rel 1e-2).  The peer-memory exchange also runs steps of both
+parities and two steps captured in a CUDA graph and replayed.  Needs two
+GPUs; skipped otherwise."""
 
 import os
 import socket
@@ -23,7 +25,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cfg_name, errq):
+def _worker(rank, world, port, cfg_name, mode, errq):
     try:
         import datetime
         from dataclasses import replace
@@ -62,13 +64,21 @@ def _worker(rank, world, port, cfg_name, errq):
                     q_max=cfg.q_max, tile_m=global_tile_m(T, k, cfg.E))
         per = T // world
         sl = slice(rank * per, (rank + 1) * per)
+        h_in = d["hidden"][sl].contiguous()
+        i_in = d["topk_ids"][sl].contiguous()
+        w_in = d["topk_weights"][sl].contiguous()
+        if mode == "p2p":
+            moe.enable_peer_exchange(per, cfg.K, k, dt)
         tr = {}
-        out = moe.forward(d["hidden"][sl].contiguous(), d["topk_ids"][sl].contiguous(),
-                          d["topk_weights"][sl].contiguous(), trace=tr)
+        out = moe.forward(h_in, i_in, w_in, trace=tr)
         torch.cuda.synchronize()
         ref = full_out[sl].float()
-        rel = ((out.float() - ref).abs().max() / ref.abs().max()).item()
-        assert rel <= 1e-2, f"rank {rank}: EP output max-abs-rel {rel:.3e} > 1e-2"
+
+        def check(o, what):
+            rel = ((o.float() - ref).abs().max() / ref.abs().max()).item()
+            assert rel <= 1e-2, f"rank {rank} {what}: EP output max-abs-rel {rel:.3e} > 1e-2"
+
+        check(out, "first step")
         assert tr["tile_m"] == full_tr["tile_m"]
         leo, feo = tr["eft"].cpu(), full_tr["eft"].cpu()
         for le in range(ep.n_local):
@@ -81,6 +91,25 @@ def _worker(rank, world, port, cfg_name, errq):
                     assert full_tr[name] is None
                     continue
                 assert torch.equal(tr[name][a:b], full_tr[name][fa:fb]), f"{name} of expert {e}"
+        if mode == "p2p":
+            # the other step parity, eagerly; then two steps in a CUDA graph
+            first = out.clone()
+            out2 = moe.forward(h_in, i_in, w_in)
+            torch.cuda.synchronize()
+            assert torch.equal(out2, first), "second step differs"
+            o_g = torch.empty_like(first)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                moe.forward(h_in, i_in, w_in, out=o_g)
+                moe.forward(h_in, i_in, w_in, out=o_g)
+            for _ in range(3):
+                o_g.zero_()
+                dist.barrier()
+                g.replay()
+                torch.cuda.synchronize()
+                assert torch.equal(o_g, first), "graph replay differs"
+            del g
+            moe.p2p.close()
         assert pkg._lib.device_error(rank) == 0
         dist.barrier()
         dist.destroy_process_group()
@@ -89,14 +118,15 @@ def _worker(rank, world, port, cfg_name, errq):
         raise
 
 
+@pytest.mark.parametrize("mode", ["nccl", "p2p"])
 @pytest.mark.parametrize("cfg_name", ["mid", "default"])
-def test_ep_two_gpus_matches_single_gpu(cfg_name):
+def test_ep_two_gpus_matches_single_gpu(cfg_name, mode):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, cfg_name, errq))
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, cfg_name, mode, errq))
              for r in range(WORLD)]
     for p in procs:
         p.start()
