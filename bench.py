@@ -56,6 +56,8 @@ def parse_args():
     ap.add_argument("--config", default="default")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: expert-parallel exchange over NVLink peer memory or NCCL")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N eager forwards only (for ncu launch lists); no JSON")
     return ap.parse_args()
@@ -331,7 +333,9 @@ def w13_algorithmic_bytes(cfg, tr):
 
 
 def run_ours_ep(args, world, rank, local):
-    """Expert-parallel forward over ``world`` GPUs (NCCL all-to-all)."""
+    """Expert-parallel forward over ``world`` GPUs: the NVLink peer-memory
+    exchange with every step a CUDA-graph replay (default), or the NCCL
+    all-to-all exchange, eagerly (``--ep-exchange nccl``)."""
     from dataclasses import replace
     import int8blockwisegemm_b200 as pkg
     from int8blockwisegemm_b200.ep import EPMoE, ExpertParallel, global_tile_m
@@ -356,24 +360,48 @@ def run_ours_ep(args, world, rank, local):
     wts = inp["topk_weights"][sl].to(dev)
     out = torch.empty_like(hidden)
     ops_per_step = 2 * T * k * (2 * cfg.N) * cfg.K + 2 * T * k * cfg.K * cfg.N
+    p2p = args.ep_exchange == "p2p"
+    if p2p:
+        moe.enable_peer_exchange(T, cfg.K, k, hidden.dtype)
 
     if args.profile_steps:
         for _ in range(args.profile_steps):
             moe.forward(hidden, ids, wts, out)
         torch.cuda.synchronize()
+        if p2p:
+            moe.p2p.close()
         return
 
     for _ in range(max(3, args.warmup)):
         moe.forward(hidden, ids, wts, out)
     torch.cuda.synchronize()
+    graphs = []
+    if p2p:
+        # one graph per step parity (the exchange alternates output buffers);
+        # step i replays graphs[i % 2]
+        for _ in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                moe.forward(hidden, ids, wts, out)
+            graphs.append(g)
+        for i in range(max(3, args.warmup)):
+            graphs[i % 2].replay()
+        torch.cuda.synchronize()
+
+    def step(i):
+        if graphs:
+            graphs[i % 2].replay()
+        else:
+            moe.forward(hidden, ids, wts, out)
+
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier(world)
         torch.cuda.synchronize()
         e0.record(s)
-        for _ in range(args.steps):
-            moe.forward(hidden, ids, wts, out)
+        for i in range(args.steps):
+            step(i)
         e1.record(s)
         torch.cuda.synchronize()
         barrier(world)
@@ -420,8 +448,14 @@ def run_ours_ep(args, world, rank, local):
           "workspace13": torch.empty(R_buf * 2 * cfg.N, dtype=hidden.dtype, device=dev)}
     t_gemm = max_over_ranks(time_w13_gemm(pkg, cfg, st, tr), world)
     gemm_bytes = w13_algorithmic_bytes(cfg, tr)
+    R_loc = int(tr["eft"][-1])
     hbm, _, src = measured_peaks()
     achieved = gemm_bytes / t_gemm / 1e9
+    del graphs
+    if p2p:
+        moe.p2p.close()
+    exch = ("NVLink peer-memory dispatch and combine (CUDA IPC, no NCCL call per step)" if p2p
+            else "NCCL all-to-all dispatch and combine")
     line = {
         "metric": METRIC, "value": world * ops_per_step * args.steps / dt / 1e12, "unit": "TOPS",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -430,14 +464,16 @@ def run_ours_ep(args, world, rank, local):
         "config": {"workload": f"{cfg.name}: T={cfg.T} tokens per rank (global {gcfg.T}),"
                                f"K={cfg.K},N={cfg.N},E={cfg.E},top{k},{cfg.dtype} activations, "
                                f"fused permute+quant and SiLU+quant",
-                   "parallelism": f"ep{world}: experts split contiguously, NCCL all-to-all "
-                                  "dispatch and combine",
+                   "parallelism": f"ep{world}: experts split contiguously, {exch}",
                    "global_batch_tokens": gcfg.T,
                    "l2": "no flush: weights+activations exceed the 126 MB L2",
-                   "timing": "eager EP forward (dispatch sizes come from host-side counts), "
-                             "CUDA events, max over ranks"},
+                   "timing": ("every step a CUDA-graph replay of the whole EP step" if p2p else
+                              "eager EP forward (dispatch sizes come from host-side counts)")
+                             + ", CUDA events, max over ranks"},
         "clocks": clocks,
-        "gpu_launches": 12 * args.steps,  # ep_plan, ep_pack, ep_combine + the 9 of the local forward
+        # p2p: ep_plan, begin, dispatch, wait, ready, combine; nccl: ep_plan, ep_pack,
+        # ep_combine; plus the 9 of the local forward
+        "gpu_launches": (15 if p2p else 12) * args.steps,
         "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel (w13, local experts)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": src, "traffic": None, "algorithmic_bytes": gemm_bytes,
