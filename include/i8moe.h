@@ -62,11 +62,13 @@ size_t i8moe_route_workspace_size(int64_t n_rows, int64_t n_expert);
  * by expert id:
  *   expert_first_token_offset[n_local_expert+1] (int64),
  *   inv_permuted_idx[n_token*topk]  (source expanded row -> destination),
- *   permuted_idx[n_token*topk]      (destination -> source; only rows below
- *       expert_first_token_offset[n_local_expert] are written when
- *       expert_map != NULL, every row otherwise).
+ *   permuted_idx[n_token*topk]      (destination -> source; slots past
+ *       expert_first_token_offset[n_local_expert] -- rows of no local
+ *       expert, when expert_map != NULL -- get the sentinel n_token*topk,
+ *       the value the reference pre-fills them with).
  * token_expert_indices supplies the value sorted with each key (the
- * reference passes arange).  expert_map (nullable, [n_expert]) remaps
+ * reference passes arange; NULL means arange).  expert_map (nullable,
+ * [n_expert]) remaps
  * global ids for expert parallelism as the reference does.  `workspace` must
  * hold i8moe_route_workspace_size() bytes. */
 int i8moe_moe_permute_metadata(const int32_t* topk_ids, const int32_t* token_expert_indices,

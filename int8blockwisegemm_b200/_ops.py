@@ -68,7 +68,7 @@ SCHEMAS = {
     "silu_and_mul": "silu_and_mul(Tensor! out, Tensor input) -> ()",
     # ---- extensions (no reference counterpart) ----
     "moe_route_for_gemm":
-        "moe_route_for_gemm(Tensor topk_ids, Tensor token_expert_indices, Tensor? expert_map, "
+        "moe_route_for_gemm(Tensor topk_ids, Tensor? token_expert_indices, Tensor? expert_map, "
         "int n_expert, int n_local_expert, int topk, Tensor! expert_first_token_offset, "
         "Tensor! inv_permuted_idx, Tensor! permuted_idx, Tensor! expert_offsets, "
         "Tensor! problem_sizes13, Tensor! problem_sizes2, Tensor! scale_offsets, int n_out1, "
@@ -294,11 +294,12 @@ def _permute(inp, topk_ids, tei, emap, n_expert, n_local, topk, pin, eft, inv, p
 
 def _route_for_gemm(topk_ids, tei, emap, n_expert, n_local, topk, eft, inv, pidx, eo32, ps1,
                     ps2, so, n_out1, k1, n_out2, k2, tile_m):
-    _check_permute_common(topk_ids, tei, eft, inv, n_local)
+    # token_expert_indices may be omitted: it is arange(n_token * topk)
+    _check_permute_common(topk_ids, tei if tei is not None else inv, eft, inv, n_local)
     n_token = topk_ids.size(0)
     ws = _route_ws(n_token * topk, n_expert, topk_ids.device)
     with torch.cuda.device(topk_ids.device):
-        call("i8moe_moe_route_for_gemm", topk_ids.data_ptr(), tei.data_ptr(), _ptr(emap),
+        call("i8moe_moe_route_for_gemm", topk_ids.data_ptr(), _ptr(tei), _ptr(emap),
              n_token, topk, n_expert, n_local, eft.data_ptr(), inv.data_ptr(), pidx.data_ptr(),
              eo32.data_ptr(), ps1.data_ptr(), ps2.data_ptr(), so.data_ptr(), n_out1, k1, n_out2,
              k2, tile_m, ws.data_ptr(), ws.numel(), _stream(topk_ids))

@@ -373,13 +373,16 @@ __global__ void __launch_bounds__(kThreads) route_scatter(RouteArgs a, int check
       wcnt[warp * a.nb + b] = 0;
     }
     if (valid) {
-      const int value = __ldg(a.values + i);
+      // token_expert_indices is arange in the reference; null means exactly that
+      const int value = a.values != nullptr ? __ldg(a.values + i) : i;
       if (value >= 0 && value < a.R) {
         a.inv[value] = dest;
       } else {
         atomicOr(&g_err_route, kErrBadIndex);
       }
-      if (dest < limit) a.pidx[dest] = value;
+      // every slot is written once: the row, or past the local experts' rows
+      // the sentinel n_token * topk the reference pre-fills permuted_idx with
+      a.pidx[dest] = dest < limit ? value : a.R;
     }
     __syncthreads();
   }

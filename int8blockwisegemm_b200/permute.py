@@ -60,13 +60,19 @@ def moe_route_for_gemm(topk_ids, n_token: int, n_expert: int, n_local_expert: in
              scale_offsets_i32 [E+1])."""
     topk = topk_ids.size(1)
     dev = topk_ids.device
-    tei, eft, pidx, inv = _alloc(n_token, topk, n_local_expert, dev)
+    # the routing kernels write every permuted_idx slot (sentinel included)
+    # and take token_expert_indices as arange when it is omitted: no
+    # pre-fill launches on this path
+    rows = n_token * topk
+    eft = torch.empty(n_local_expert + 1, dtype=torch.int64, device=dev)
+    pidx = torch.empty(rows, dtype=torch.int32, device=dev)
+    inv = torch.empty((n_token, topk), dtype=torch.int32, device=dev)
     eo = torch.empty(n_local_expert + 1, dtype=torch.int32, device=dev)
     ps1 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)
     ps2 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)
     so = torch.empty(n_local_expert + 1, dtype=torch.int32, device=dev)
     torch.ops.int8_hybrid_moe.moe_route_for_gemm(
-        topk_ids.to(torch.int32), tei, expert_map, n_expert, n_local_expert, topk, eft, inv,
+        topk_ids.to(torch.int32), None, expert_map, n_expert, n_local_expert, topk, eft, inv,
         pidx, eo, ps1, ps2, so, n_out1, k1, n_out2, k2, tile_m)
     return eft, inv.flatten(), pidx, eo, ps1, ps2, so
 
@@ -102,7 +108,9 @@ def router_route_for_gemm(logits, topk: int, n_local_expert: int, expert_map, n_
     dev = logits.device
     ids = torch.empty(T, topk, dtype=torch.int32, device=dev)
     w = torch.empty(T, topk, dtype=torch.float32, device=dev)
-    tei, eft, pidx, inv = _alloc(T, topk, n_local_expert, dev)
+    eft = torch.empty(n_local_expert + 1, dtype=torch.int64, device=dev)
+    pidx = torch.empty(T * topk, dtype=torch.int32, device=dev)
+    inv = torch.empty((T, topk), dtype=torch.int32, device=dev)
     eo = torch.empty(n_local_expert + 1, dtype=torch.int32, device=dev)
     ps1 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)
     ps2 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)
@@ -114,7 +122,7 @@ def router_route_for_gemm(logits, topk: int, n_local_expert: int, expert_map, n_
     with torch.cuda.device(dev):
         call("i8moe_router_route_for_gemm", logits.data_ptr(),
              bias.data_ptr() if bias is not None else None, T, E, topk, ids.data_ptr(),
-             w.data_ptr(), tei.data_ptr(), emap.data_ptr() if emap is not None else None,
+             w.data_ptr(), None, emap.data_ptr() if emap is not None else None,
              n_local_expert, eft.data_ptr(), inv.data_ptr(), pidx.data_ptr(), eo.data_ptr(),
              ps1.data_ptr(), ps2.data_ptr(), so.data_ptr(), n_out1, k1, n_out2, k2, tile_m,
              ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
