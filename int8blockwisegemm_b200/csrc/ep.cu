@@ -229,7 +229,7 @@ __device__ bool wait_flags(const P2PArgs& a, int kind, uint64_t ep) {
 }
 enum { kFlagCounts = 0, kFlagRows = 1, kFlagOut = 2 };
 
-__global__ void ep_p2p_begin(P2PArgs a) {
+__global__ void ep_p2p_begin(const __grid_constant__ P2PArgs a) {
   uint64_t* e = reinterpret_cast<uint64_t*>(a.base[a.rank] + a.off_epoch);
   *e = *e + 1;
 }
@@ -246,7 +246,7 @@ __device__ void p2p_offsets(const P2PArgs& a, int* off_to) {
   }
 }
 
-__global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(P2PArgs a, const uint4* __restrict__ hidden,
+__global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(const __grid_constant__ P2PArgs a, const uint4* __restrict__ hidden,
                                                               const int32_t* __restrict__ ids,
                                                               const float* __restrict__ w,
                                                               const int32_t* __restrict__ list,
@@ -293,7 +293,21 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(P2PArgs a, const u
     }
     const uint4* src = hidden + static_cast<int64_t>(t) * chunks;
     uint4* dst = reinterpret_cast<uint4*>(a.base[d] + a.off_rows) + row * chunks;
-    for (int64_t c = lane; c < chunks; c += 32) dst[c] = __ldg(src + c);
+    // all of a lane's loads of the row go out before its peer stores
+    constexpr int kU = 8;
+    for (int64_t c0 = 0; c0 < chunks; c0 += 32 * kU) {
+      uint4 v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t c = c0 + u * 32 + lane;
+        if (c < chunks) v[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t c = c0 + u * 32 + lane;
+        if (c < chunks) dst[c] = v[u];
+      }
+    }
     if (lane < a.k) {
       reinterpret_cast<int32_t*>(a.base[d] + a.off_ids)[row * a.k + lane] =
           __ldg(ids + static_cast<int64_t>(t) * a.k + lane);
@@ -316,7 +330,7 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(P2PArgs a, const u
 
 // Until every source has posted its rows; then the receive rows past the
 // received ones get a non-local expert id and weight 0.
-__global__ void __launch_bounds__(256) ep_p2p_wait_kernel(P2PArgs a) {
+__global__ void __launch_bounds__(256) ep_p2p_wait_kernel(const __grid_constant__ P2PArgs a) {
   __shared__ int s_ok;
   const uint64_t ep = my_epoch(a);
   if (threadIdx.x == 0) s_ok = wait_flags(a, kFlagRows, ep) ? 1 : 0;
@@ -338,7 +352,7 @@ __global__ void __launch_bounds__(256) ep_p2p_wait_kernel(P2PArgs a) {
 
 // This rank's local forward output (a previous kernel on the stream) is
 // complete: raise the "output ready" flag at every peer.
-__global__ void ep_p2p_ready_kernel(P2PArgs a) {
+__global__ void ep_p2p_ready_kernel(const __grid_constant__ P2PArgs a) {
   const uint64_t ep = my_epoch(a);
   __threadfence_system();
   if (threadIdx.x < a.P) st_release_sys(flag_ptr(a, threadIdx.x, kFlagOut, a.rank), ep);
@@ -347,10 +361,11 @@ __global__ void ep_p2p_ready_kernel(P2PArgs a) {
 // out[t] = dtype(sum over destinations d in rank order of d's output row
 // off_to[d] + pos[t, d]), fp32 accumulation, rows read from peer memory.
 template <typename T>
-__global__ void __launch_bounds__(256) ep_p2p_combine_kernel(P2PArgs a, const int32_t* __restrict__ pos,
+__global__ void __launch_bounds__(256) ep_p2p_combine_kernel(const __grid_constant__ P2PArgs a, const int32_t* __restrict__ pos,
                                                              T* __restrict__ out) {
   constexpr int EPC = 8;
   __shared__ int s_off[kMaxRanks];
+  __shared__ int64_t s_row[kMaxRanks];  // this token's row in destination d's output, or -1
   __shared__ int s_ok;
   const uint64_t ep = my_epoch(a);
   if (threadIdx.x == 0) s_ok = wait_flags(a, kFlagOut, ep) ? 1 : 0;
@@ -360,27 +375,38 @@ __global__ void __launch_bounds__(256) ep_p2p_combine_kernel(P2PArgs a, const in
   __syncthreads();
   const int chunks = a.K / EPC;
   for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
-    int64_t rows[kMaxRanks];
-    int owner[kMaxRanks];
-    int nr = 0;
-    for (int d = 0; d < a.P; ++d) {
+    if (threadIdx.x < a.P) {
+      const int d = threadIdx.x;
       const int p = __ldg(pos + static_cast<int64_t>(t) * a.P + d);
-      if (p >= 0 && s_off[d] + p < a.C) {
-        rows[nr] = s_off[d] + p;
-        owner[nr++] = d;
-      }
+      s_row[d] = (p >= 0 && s_off[d] + p < a.C) ? static_cast<int64_t>(s_off[d] + p) : -1;
     }
+    __syncthreads();
     for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
       float acc[EPC];
 #pragma unroll
       for (int i = 0; i < EPC; ++i) acc[i] = 0.f;
-      for (int r = 0; r < nr; ++r) {
-        const T* src = reinterpret_cast<const T*>(a.base[owner[r]] + a.off_out + a.par * a.out_bytes) +
-                       rows[r] * a.K;
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + c);  // peer memory, via L2
-        const T* x = reinterpret_cast<const T*>(&v);
+      // up to eight destinations' loads in flight together, then summed in rank order
+      constexpr int kU = 8;
+      for (int d0 = 0; d0 < a.P; d0 += kU) {
+        uint4 v[kU];
 #pragma unroll
-        for (int i = 0; i < EPC; ++i) acc[i] += Num<T>::to_f(x[i]);
+        for (int u = 0; u < kU; ++u) {
+          const int d = d0 + u;
+          if (d < a.P && s_row[d] >= 0) {
+            const T* src = reinterpret_cast<const T*>(a.base[d] + a.off_out + a.par * a.out_bytes) +
+                           s_row[d] * a.K;
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(src) + c);  // peer memory, via L2
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int d = d0 + u;
+          if (d < a.P && s_row[d] >= 0) {
+            const T* x = reinterpret_cast<const T*>(&v[u]);
+#pragma unroll
+            for (int i = 0; i < EPC; ++i) acc[i] += Num<T>::to_f(x[i]);
+          }
+        }
       }
       uint4 o;
       T* y = reinterpret_cast<T*>(&o);
@@ -388,6 +414,7 @@ __global__ void __launch_bounds__(256) ep_p2p_combine_kernel(P2PArgs a, const in
       for (int i = 0; i < EPC; ++i) y[i] = Num<T>::from_f(acc[i]);
       reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * a.K)[c] = o;
     }
+    __syncthreads();  // s_row is rewritten for the next token
   }
 }
 
