@@ -72,3 +72,29 @@ def test_noalloc_rejects_problems_above_its_fixed_scratch():
     assert rc == -1
     msg = _lib.last_error()
     assert "fixed" in msg and "i8moe_moe_permute_metadata" in msg
+
+
+def test_peer_exchange_region_layout():
+    """The peer-exchange region layout (a host-side computation): every part
+    256-byte aligned, disjoint, inside the region, and bad shapes rejected."""
+    import ctypes
+    from int8blockwisegemm_b200 import _lib
+    from int8blockwisegemm_b200.ep import _Layout
+    lib = _lib.LIB
+    P, T, k, K = 8, 8192, 8, 2048
+    lay = _Layout()
+    assert lib.i8moe_ep_p2p_region_bytes(P, P * T, k, K, 2, ctypes.addressof(lay)) == 0
+    C = P * T
+    parts = [(lay.off_rows, C * K * 2), (lay.off_ids, C * k * 4), (lay.off_w, C * k * 4),
+             (lay.off_out, 2 * lay.out_bytes), (lay.off_inbox, 2 * P * P * 4),
+             (lay.off_flags, 3 * P * 8), (lay.off_epoch, 12)]
+    assert lay.out_bytes >= C * K * 2
+    end = 0
+    for off, size in parts:
+        assert off % 256 == 0 and off >= end, (off, end)
+        end = off + size
+    assert end <= lay.bytes
+    assert lib.i8moe_ep_p2p_region_bytes(33, 33, k, K, 2, ctypes.addressof(lay)) == -1
+    assert "ranks" in _lib.last_error()
+    assert lib.i8moe_ep_p2p_region_bytes(P, C, k, K, 4, ctypes.addressof(lay)) == -1
+    assert lib.i8moe_ep_p2p_region_bytes(P, C, 33, K, 2, ctypes.addressof(lay)) == -1
