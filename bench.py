@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark of the INT8 hybrid MoE forward on B200 (BASELINE metric:
+"""Benchmark of the INT8 hybrid MoE forward on B200 (headline metric:
 "MoE fwd ms & INT8 TOPS (M=8192,K=2048,N=512,E=256,top8)").
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -9,7 +9,8 @@ One step = one forward pass (routing -> permute+quant -> w13 GEMM ->
 SiLU*up+requant -> w2 GEMM -> weighted unpermute) over one batch of the
 configuration's tokens.  ``value`` is whole-job INT8 TOPS (GEMM ops of all
 ranks / max-over-ranks device time); ``ms_per_step`` is the forward latency.
-Inputs are synthetic (seeded, BASELINE distributions) and resident in HBM;
+Inputs are synthetic (seeded, with the distributions workloads.py documents)
+and resident in HBM;
 the whole forward is replayed from a CUDA graph.  ``e2e`` times the public
 entry point (cutlass_runner._run_cutlass_int8_hybrid_grouped_moe) called
 eagerly with the per-step inputs copied from pinned host memory and the
@@ -44,11 +45,11 @@ sys.path.insert(0, str(ROOT))
 
 import torch  # noqa: E402
 
-METRIC = "MoE fwd INT8 TOPS (M=8192,K=2048,N=512,E=256,top8)"  # BASELINE's, the default config
+METRIC = "MoE fwd INT8 TOPS (M=8192,K=2048,N=512,E=256,top8)"  # the headline, default config
 
 
 def metric_name(cfg) -> str:
-    """BASELINE's metric for the default config; the same metric named with
+    """The headline metric for the default config; the same metric named with
     the shape of any other configuration."""
     if cfg.name == "default":
         return METRIC
@@ -242,8 +243,8 @@ def run_reference(args, world, rank):
 def make_problem(cfg, inp, dev):
     import int8blockwisegemm_b200 as pkg
     r = pkg.cutlass_runner
-    r._USE_FUSED_PERMUTE_QUANT_W1 = True   # BASELINE: fused permute+quant on
-    r._USE_FUSED_SILU_QUANT_W2 = True      # BASELINE: fused SiLU+quant on
+    r._USE_FUSED_PERMUTE_QUANT_W1 = True   # benchmark configuration: fused permute+quant
+    r._USE_FUSED_SILU_QUANT_W2 = True      # and fused SiLU+quant
     dt = {"bf16": torch.bfloat16, "fp16": torch.float16}[cfg.dtype]
     T, k = inp["topk_ids"].shape
     R = T * k

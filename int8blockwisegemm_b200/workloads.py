@@ -52,7 +52,7 @@ class MoEConfig:
 
 
 CONFIGS = {
-    # BASELINE configs[0]: tiny CPU-runnable reference case.
+    # configs[0]: tiny CPU-runnable reference case.
     "tiny": MoEConfig("tiny", T=64, K=256, N=128, E=8, topk=2, sg=2),
     # default Qwen3-MoE-like benchmark shape (the headline).
     "default": MoEConfig("default", T=8192, K=2048, N=512, E=256, topk=8),

@@ -388,7 +388,10 @@ def weight_quant_cases(ref_root: Path, mods):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("INT8_HYBRID_MOE_REFERENCE_SRC"),
+                    required="INT8_HYBRID_MOE_REFERENCE_SRC" not in os.environ,
+                    help="the reference's source tree (its int8_hybrid_moe package and "
+                         "benchmark script)")
     ap.add_argument("--only", choices=["all", "weights"], default="all")
     args = ap.parse_args()
     mods = _load_reference(Path(args.ref))

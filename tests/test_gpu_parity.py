@@ -11,7 +11,8 @@ Tolerances:
     and at most one step (fp32 storage: a few float32 ulp);
   * unpermute: the oracle emulates fp32 FMA in float64 (double rounding can
     differ by one float32 ulp), so one bf16/fp16 ulp on a tiny fraction;
-  * final MoE output: max|y - ref| / max|ref| <= 1e-2.
+  * final MoE output: max|y - ref| / max|ref| <= 1e-2 (the path's stated
+    floating-point tolerance).
 """
 
 import numpy as np
@@ -436,7 +437,7 @@ def test_forward_cuda_graph_replay(m):
 
 
 def test_forward_default_config_stagewise(m):
-    """BASELINE configs[1] at full size.  Every stage is checked against the
+    """The default (headline) configuration at full size.  Every stage is checked against the
     oracle applied to the device's own previous-stage output (GEMMs on a sample
     of experts), plus the end-to-end output tolerance on sampled tokens."""
     cfg, inp = inputs("default")
