@@ -95,14 +95,19 @@ def _worker(rank, world, port, cfg_name, only_rank0_experts, errq):
         raise
 
 
-@pytest.mark.parametrize("cfg_name,only_rank0", [("tiny", False), ("mid", False),
-                                                  ("tiny", True)])
-def test_ep_two_gloo_ranks_match_single_process(cfg_name, only_rank0):
+@pytest.mark.parametrize("world,cfg_name,only_rank0", [(WORLD, "tiny", False),
+                                                        (WORLD, "mid", False),
+                                                        (WORLD, "tiny", True),
+                                                        (4, "tiny", False), (4, "mid", False)])
+def test_ep_gloo_ranks_match_single_process(world, cfg_name, only_rank0):
+    """world gloo ranks on CPU: the exchange orders every expert's rows as one
+    process would (bit-identical activations, accumulators and outputs per
+    expert), the combined output is within 1e-2 of the single-process one."""
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, cfg_name, only_rank0, errq))
-             for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_name, only_rank0, errq))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
