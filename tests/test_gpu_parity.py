@@ -429,6 +429,39 @@ def test_forward_against_reference_golden(m, gname, cname, fp, fs, ep, fuse_w13,
     assert np.abs(o - g["out"]).max() / np.abs(g["out"]).max() <= 1e-2
 
 
+@PAIRS
+@pytest.mark.parametrize("fuse_w13", [False, True], ids=["w13-store", "w13-silu-epilogue"])
+def test_forward_decode_config_against_oracle(m, fuse_w13, cta_pairs):
+    """The decode configuration (128 tokens over 256 experts, top-8: a few
+    rows per expert, most of them in one ragged tile, the tile_m 64 variant)
+    against the oracle, stage by stage: routing maps, int8 activations and
+    their Q/F bit-exact, a2q within one step on rare elements (SiLU rounding),
+    the output within 1e-2."""
+    cfg, inp = inputs("decode")
+    tr = {}
+    out = run_forward(m, cfg, inp, True, True, trace=tr, fuse_w13=fuse_w13)
+    npi = {k: npf(v) for k, v in inp.items()}
+    ref_tr = ref.moe_forward(npi["hidden"], npi["w13"], npi["w2"], npi["topk_ids"],
+                             npi["topk_weights"], npi["w13_q"], npi["w13_f"], npi["w2_q"],
+                             npi["w2_f"], dtype=cfg.dtype, global_num_experts=cfg.E,
+                             super_group_size=cfg.sg, q_max=cfg.q_max, trace=True)
+    assert tr["tile_m"] == ref_tr.tile_m == 64
+    np.testing.assert_array_equal(npf(tr["eft"]), ref_tr.offsets)
+    np.testing.assert_array_equal(npf(tr["inv"]), ref_tr.inv.reshape(-1))
+    v = int(ref_tr.offsets[-1])
+    rows = ref_tr.a1_Q.shape[0]
+    np.testing.assert_array_equal(npf(tr["a1q"])[:v], ref_tr.a1q)
+    np.testing.assert_array_equal(npf(tr["a1_Q"])[:rows], ref_tr.a1_Q)
+    np.testing.assert_array_equal(npf(tr["a1_F"])[:rows], ref_tr.a1_F)
+    if tr["mm1"] is not None:
+        np.testing.assert_array_equal(npf(tr["mm1"])[:v], ref_tr.mm1)
+    d2 = np.abs(npf(tr["a2q"])[:v].astype(np.int32) - ref_tr.a2q.astype(np.int32))
+    assert d2.max() <= 1 and (d2 > 0).mean() < 1e-3
+    o = npf(out)
+    assert np.abs(o - ref_tr.out).max() / np.abs(ref_tr.out).max() <= 1e-2
+    assert m._lib.device_error(0) == 0
+
+
 def test_forward_cuda_graph_replay(m):
     cfg, inp = inputs("mid")
     eager = run_forward(m, cfg, inp).clone()
@@ -486,7 +519,7 @@ def test_forward_default_config_stagewise(m):
     assert ud.max() <= 1 and (ud > 0).mean() < 1e-3
 
 
-FUSED_W13_CASES = ["tiny", "ragged", "tm128", "mid", "large_small", "default"]
+FUSED_W13_CASES = ["tiny", "ragged", "tm128", "mid", "decode", "large_small", "default"]
 
 
 @PAIRS
