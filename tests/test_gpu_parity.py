@@ -469,11 +469,13 @@ def test_forward_cuda_graph_replay(m):
     assert torch.equal(eager, replay)
 
 
-def test_forward_default_config_stagewise(m):
-    """The default (headline) configuration at full size.  Every stage is checked against the
-    oracle applied to the device's own previous-stage output (GEMMs on a sample
-    of experts), plus the end-to-end output tolerance on sampled tokens."""
-    cfg, inp = inputs("default")
+@pytest.mark.parametrize("cname", ["default", "skewed"])
+def test_forward_full_config_stagewise(m, cname):
+    """A benchmark configuration at full size: the default (headline) one and
+    the skewed-routing one (hottest expert ~10x the mean load).  Every stage
+    is checked against the oracle applied to the device's own previous-stage
+    output (GEMMs on a sample of experts, the hottest and coldest included)."""
+    cfg, inp = inputs(cname)
     tr = {}
     out = run_forward(m, cfg, inp, True, True, trace=tr, fuse_w13=False)
     T, k = inp["topk_ids"].shape
@@ -491,7 +493,9 @@ def test_forward_default_config_stagewise(m):
     np.testing.assert_array_equal(npf(tr["a1_Q"])[:Q1.shape[0]], Q1)
     np.testing.assert_array_equal(npf(tr["a1_F"])[:F1.shape[0]], F1)
     # GEMMs on a sample of experts (inputs: the device's own int8 activations)
-    sample = [0, 1, 77, 128, 255]
+    counts = eft[1:] - eft[:-1]
+    live = np.nonzero(counts > 0)[0]
+    sample = sorted({0, 1, 77, 128, 255, int(np.argmax(counts)), int(live[np.argmin(counts[live])])})
     for e in sample:
         lo, hi = int(eft[e]), int(eft[e + 1])
         cnt = hi - lo
