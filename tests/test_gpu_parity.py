@@ -431,13 +431,14 @@ def test_forward_against_reference_golden(m, gname, cname, fp, fs, ep, fuse_w13,
 
 @PAIRS
 @pytest.mark.parametrize("fuse_w13", [False, True], ids=["w13-store", "w13-silu-epilogue"])
-def test_forward_decode_config_against_oracle(m, fuse_w13, cta_pairs):
-    """The decode configuration (128 tokens over 256 experts, top-8: a few
-    rows per expert, most of them in one ragged tile, the tile_m 64 variant)
-    against the oracle, stage by stage: routing maps, int8 activations and
-    their Q/F bit-exact, a2q within one step on rare elements (SiLU rounding),
-    the output within 1e-2."""
-    cfg, inp = inputs("decode")
+@pytest.mark.parametrize("cname,tile_m", [("decode", 64), ("mid", 128)])
+def test_forward_config_against_oracle(m, cname, tile_m, fuse_w13, cta_pairs):
+    """A whole configuration against the oracle, stage by stage: routing maps,
+    int8 activations and their Q/F bit-exact, a2q within one step on rare
+    elements (SiLU rounding), the output within 1e-2.  decode: 128 tokens
+    over 256 experts, top-8 -- a few rows per expert, most in one ragged
+    tile, the tile_m 64 variant; mid: 512 tokens over 16 experts, tile_m 128."""
+    cfg, inp = inputs(cname)
     tr = {}
     out = run_forward(m, cfg, inp, True, True, trace=tr, fuse_w13=fuse_w13)
     npi = {k: npf(v) for k, v in inp.items()}
@@ -445,7 +446,7 @@ def test_forward_decode_config_against_oracle(m, fuse_w13, cta_pairs):
                              npi["topk_weights"], npi["w13_q"], npi["w13_f"], npi["w2_q"],
                              npi["w2_f"], dtype=cfg.dtype, global_num_experts=cfg.E,
                              super_group_size=cfg.sg, q_max=cfg.q_max, trace=True)
-    assert tr["tile_m"] == ref_tr.tile_m == 64
+    assert tr["tile_m"] == ref_tr.tile_m == tile_m
     np.testing.assert_array_equal(npf(tr["eft"]), ref_tr.offsets)
     np.testing.assert_array_equal(npf(tr["inv"]), ref_tr.inv.reshape(-1))
     v = int(ref_tr.offsets[-1])
