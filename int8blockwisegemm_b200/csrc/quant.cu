@@ -123,15 +123,17 @@ __global__ void __launch_bounds__(kQuantThreads, (RowsTile<T, TM, MODE>::MIN_BLO
   }
   const int cc = lane % CPR;
   const T* src = static_cast<const T*>(a.src);
-  int64_t src_off[NP];  // element offset of this thread's row in the source, -1 if none
+  // source row of this thread's row in each pass, -1 if none (32-bit: the
+  // eight rows stay in registers across the K-blocks without spilling)
+  int32_t src_row[NP];
 #pragma unroll
   for (int j = 0; j < NP; ++j) {
     const int r = j * RPP + warp * RPW + lane / CPR;
-    src_off[j] = -1;
+    src_row[j] = -1;
     if (r < rows) {
-      int64_t srow = row_start + r;
+      int srow = row_start + r;
       if (MODE == kGather) srow = __ldg(a.pidx + srow) / a.topk;
-      src_off[j] = srow * a.src_stride;
+      src_row[j] = srow;
     }
   }
   const int kb1 = min(kb0 + kKbPerCta, a.Kb);
@@ -143,8 +145,8 @@ __global__ void __launch_bounds__(kQuantThreads, (RowsTile<T, TM, MODE>::MIN_BLO
 #pragma unroll
     for (int j = 0; j < NP; ++j) {
       v[j] = make_uint4(0u, 0u, 0u, 0u);
-      if (src_off[j] >= 0 && col_ok) {
-        const T* p = src + src_off[j] + col;
+      if (src_row[j] >= 0 && col_ok) {
+        const T* p = src + static_cast<int64_t>(src_row[j]) * a.src_stride + col;
         if (MODE == kSilu) {
           const uint4 g = __ldg(reinterpret_cast<const uint4*>(p));
           const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + a.K));
