@@ -265,15 +265,18 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(const __grid_const
   }
   if (threadIdx.x == 0) s_ok = wait_flags(a, kFlagCounts, ep) ? 1 : 0;
   __syncthreads();
-  if (!s_ok) return;
-  p2p_offsets(a, s_off);
+  // A CTA whose wait gave up (the error word now says so) copies no rows but
+  // still counts itself below: the persistent completion counter must see
+  // every CTA of every launch, or a later step's "rows posted" flag would be
+  // raised before all of that step's rows are stored.
+  if (s_ok) p2p_offsets(a, s_off);
   if (threadIdx.x == 0) {
     int o = 0;
     for (int d = 0; d < a.P; ++d) {
       s_seg[d] = o;
       o += __ldg(counts + d);
     }
-    s_seg[a.P] = o;
+    s_seg[a.P] = s_ok ? o : 0;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;

@@ -621,6 +621,8 @@ int launch_route_noalloc(const int32_t* topk_ids, const int32_t* tei, const int3
                          int64_t* eft, int32_t* inv, int32_t* pidx, cudaStream_t st) {
   I8_REQUIRE(n_token >= 0 && topk > 0, "moe_permute: bad n_token/topk");
   I8_REQUIRE(n_expert >= 1 && n_expert <= 2048, "moe_permute: n_expert must be in [1, 2048]");
+  // bound the row count before forming it, so n_token * topk cannot overflow
+  I8_REQUIRE(n_token <= INT32_MAX / topk, "moe_permute: n_token * topk must fit in int32");
   const size_t need = route_ws_bytes(n_token * topk, n_expert);
   I8_REQUIRE(need <= kNoAllocScratchBytes,
              "moe_permute_metadata_noalloc: %lld rows of %lld experts need %zu bytes of routing "

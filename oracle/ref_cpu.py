@@ -431,8 +431,6 @@ def hybrid_grouped_gemm(A, QA, FA, B, QB, FB, expert_offsets, problem_sizes,
     else:
         so = np.asarray(scale_offsets, np.int64)
     jn = np.arange(N) // TILE_N_SCALE
-    b_pad = np.zeros((E, N, Kt * TILE_K), np.float32)
-    b_pad[:, :, pad:] = B
     for e in range(E):
         m_e = int(ps[e, 0])
         if m_e <= 0:
@@ -440,8 +438,10 @@ def hybrid_grouped_gemm(A, QA, FA, B, QB, FB, expert_offsets, problem_sizes,
         r0 = int(eo[e])
         a_e = np.zeros((m_e, Kt * TILE_K), np.float32)
         a_e[:, pad:] = A[r0:r0 + m_e]
+        b_e = np.zeros((N, Kt * TILE_K), np.float32)  # one expert at a time (memory)
+        b_e[:, pad:] = B[e]
         a_t = a_e.reshape(m_e, Kt, TILE_K).transpose(1, 0, 2)
-        b_t = b_pad[e].reshape(N, Kt, TILE_K).transpose(1, 2, 0)
+        b_t = b_e.reshape(N, Kt, TILE_K).transpose(1, 2, 0)
         P = np.matmul(a_t, b_t)  # [Kt, m_e, N]: exact (|P| < 2**24)
         P = P.astype(np.int64)
         srow = so[e] + np.arange(m_e) // tile_m

@@ -72,6 +72,11 @@ def test_noalloc_rejects_problems_above_its_fixed_scratch():
     assert rc == -1
     msg = _lib.last_error()
     assert "fixed" in msg and "i8moe_moe_permute_metadata" in msg
+    # a row count n_token * topk that does not fit in int32 is rejected before
+    # it is formed
+    rc = lib.i8moe_moe_permute_metadata_noalloc(None, None, None, 2**40, 8, 8, 8, None, None,
+                                                None, None)
+    assert rc == -1 and "int32" in _lib.last_error()
 
 
 def test_peer_exchange_region_layout():

@@ -141,3 +141,54 @@ def test_ep_two_gpus_matches_single_gpu(cfg_name, mode):
     assert not alive, "EP ranks did not finish"
     assert not errs, "\n".join(errs)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def test_p2p_dispatch_peer_timeout_one_gpu():
+    """A peer that never answers, on one GPU: rank 1's region is a second
+    local region that nothing writes, so rank 0's dispatch waits for segment
+    lengths that never come.  Every wait gives up after its bound (2 s), the
+    kernel returns, the device error word reports the peer timeout, and the
+    persistent CTA completion counter is back at zero after each such step
+    (every CTA counts itself even when its wait failed), so a later step
+    cannot raise its "rows posted" flag early."""
+    import ctypes
+
+    import int8blockwisegemm_b200 as pkg
+    from int8blockwisegemm_b200._lib import call
+    from int8blockwisegemm_b200.ep import _Layout, _P2PDesc
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    P, T, k, K = 2, 64, 4, 256
+    lay = _Layout()
+    call("i8moe_ep_p2p_region_bytes", P, P * T, k, K, 2, ctypes.addressof(lay))
+    regions = [torch.zeros(lay.bytes, dtype=torch.uint8, device=dev) for _ in range(P)]
+    desc = _P2PDesc()
+    for d in range(P):
+        desc.bases[d] = regions[d].data_ptr()
+    desc.n_rank, desc.rank, desc.n_token, desc.capacity = P, 0, T, P * T
+    desc.topk, desc.n_hidden, desc.elem_bytes, desc.pad_expert = k, K, 2, 8
+    desc.layout = lay
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, 16, (T, k), generator=g, dtype=torch.int32).to(dev)
+    w = torch.rand(T, k, generator=g).to(dev)
+    hidden = torch.randn(T, K, generator=g).to(torch.bfloat16).to(dev)
+    pos = torch.empty(T, P, dtype=torch.int32, device=dev)
+    lst = torch.empty(P, T, dtype=torch.int32, device=dev)
+    counts = torch.empty(P, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    pkg._lib.device_error(0, clear=True)
+    ctr_off = lay.off_epoch + 8
+    for step in range(2):
+        call("i8moe_ep_plan", ids.data_ptr(), T, k, 8, P, pos.data_ptr(), lst.data_ptr(),
+             counts.data_ptr(), st)
+        call("i8moe_ep_p2p_dispatch", ctypes.addressof(desc), step & 1, hidden.data_ptr(),
+             ids.data_ptr(), w.data_ptr(), lst.data_ptr(), counts.data_ptr(), st)
+        torch.cuda.synchronize()
+        err = pkg._lib.device_error(0, clear=True)
+        assert err & (1 << 6), f"step {step}: no peer-timeout bit in the error word ({err:#x})"
+        ctr = regions[0][ctr_off:ctr_off + 4].view(torch.int32).item()
+        assert ctr == 0, f"step {step}: CTA completion counter left at {ctr}"
+        epoch = regions[0][lay.off_epoch:lay.off_epoch + 8].view(torch.int64).item()
+        assert epoch == step + 1
+    assert pkg._lib.device_error(0) == 0
