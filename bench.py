@@ -18,11 +18,19 @@ output copied back inside the timed region.
 
 Multi-GPU (torchrun, one process per GPU): expert parallelism.  Rank r owns
 experts [r*E/N, (r+1)*E/N) and the configuration's T tokens of its own
-(global batch N*T, weak scaling); a step is one NCCL dispatch all-to-all, the
-local forward of the rows that reached the rank, and one combine all-to-all.
-The dispatch sizes its payload exchange from host-side counts, so EP steps
-run eagerly (no CUDA graph).  The timed region is bracketed by barriers and
-the reported time is the max over ranks.
+(global batch N*T, weak scaling).  A step stores every token row into the
+receive buffers of the ranks owning its experts over NVLink peer memory, runs
+the local forward over the received rows and sums the partial rows back from
+the peers' output buffers (csrc/ep.cu, ``PeerExchange``): no NCCL call and no
+host synchronisation per step, so each step is a CUDA-graph replay.
+``--ep-exchange nccl`` runs the NCCL all-to-all exchange instead (eager: its
+payload sizes come from host-side counts).  The timed region is bracketed by
+barriers and the reported time is the max over ranks.  The EP ``e2e`` is
+pipelined like the single-GPU one.
+
+Other modes: ``--breakdown`` times every kernel of one forward separately
+with its algorithmic bytes and roofline fraction; ``--int8-peak`` measures
+the dense INT8 tcgen05 peak of the device.
 
 ``--impl reference`` times the CPU restatement of the reference path
 (oracle/ref_cpu.py, numpy on the host cores) on a bounded token sample of the
@@ -69,7 +77,41 @@ def parse_args():
                     help="N>1: expert-parallel exchange over NVLink peer memory or NCCL")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N eager forwards only (for ncu launch lists); no JSON")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="time every kernel of the forward separately (plus the per-tensor "
+                         "grouped GEMM on the w13 shape) and print one JSON line")
+    ap.add_argument("--int8-peak", action="store_true",
+                    help="measure the dense INT8 tcgen05 peak (i8moe_int8_mma_peak) and exit")
     return ap.parse_args()
+
+
+def int8_mma_peak(local: int, steps: int = 40000, reps: int = 5) -> dict:
+    """Dense INT8 tensor-core peak: i8moe_int8_mma_peak timed with CUDA
+    events (best of ``reps`` launches after one warm-up), with the SM clock
+    sampled during the launches, for one CTA per SM and for CTA pairs."""
+    import ctypes
+    from int8blockwisegemm_b200 import _lib
+    s = torch.cuda.current_stream()
+    res = {}
+    for cg in (1, 2):
+        n_cta = ctypes.c_int64(0)
+        _lib.call("i8moe_int8_mma_peak", steps, cg, ctypes.addressof(n_cta), s.cuda_stream)
+        torch.cuda.synchronize()
+        best = None
+        with ClockSampler(local) as clk:
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                _lib.call("i8moe_int8_mma_peak", steps, cg, ctypes.addressof(n_cta), s.cuda_stream)
+                e1.record(s)
+                torch.cuda.synchronize()
+                t = e0.elapsed_time(e1) * 1e-3
+                best = t if best is None else min(best, t)
+        ops = 2 * 128 * 256 * 128 * steps * n_cta.value
+        res[f"cta_group_{cg}"] = {"tops": ops / best / 1e12, "seconds": best, "ctas": n_cta.value,
+                                  "clocks": clk.summary()}
+    assert _lib.device_error(local) == 0
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -341,6 +383,179 @@ def w13_algorithmic_bytes(cfg, tr):
     return b
 
 
+def _graph_time(fn, iters=20):
+    """Average device time of ``fn`` replayed ``iters`` times from one CUDA
+    graph (CUDA events on the launching stream, after warm-up)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / iters * 1e-3
+
+
+def run_breakdown(args, local):
+    """Per-kernel device times of one forward of ``--config`` with their
+    algorithmic bytes (one byte per int8 element, two per 16-bit element,
+    each tensor counted once, weights only for experts that have rows) and
+    the fraction of the measured HBM peak; INT8 TOPS for the GEMMs.  Adds the
+    per-tensor grouped GEMM (per-token x per-expert scales, the decode
+    configuration's variant) on the w13 shape, and the unfused w13 GEMM."""
+    wl = load_workloads()
+    cfg = wl.CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    inp = wl.make_inputs(cfg)
+    pkg, st, fwd = make_problem(cfg, inp, dev)
+    tr = {}
+    fwd(_trace=tr)
+    torch.cuda.synchronize()
+    T, k = inp["topk_ids"].shape
+    R = T * k
+    K, N, E = cfg.K, cfg.N, cfg.E
+    es = st["hidden"].element_size()
+    tm = tr["tile_m"]
+    eft = tr["eft"].cpu()
+    counts = eft[1:] - eft[:-1]
+    e_hit = int((counts > 0).sum())
+    rows_s = int(((counts + tm - 1).div(tm, rounding_mode="floor")).sum())
+    kb1, kb2 = -(-K // cfg.quant_block), -(-N // cfg.quant_block)
+    sg1, sg2 = -(-kb1 // cfg.sg), -(-kb2 // cfg.sg)
+    hbm, _, src = measured_peaks()
+    so = tr["scale_offsets"]
+    dt = st["hidden"].dtype
+    mm1 = st["workspace13"].flatten()[: R * 2 * N].view(R, 2 * N)
+    mm2 = st["workspace2"].flatten()[: R * K].view(R, K)
+    gemm = (pkg.ops.cutlass_int8_blockwise_hybrid_grouped if tm == 128
+            else pkg.ops.cutlass_int8_blockwise_hybrid_grouped_small)
+    g = torch.Generator().manual_seed(3)
+    row_scale = (torch.rand(R, generator=g) * 1e-2).to(dev)
+    exp_scale = torch.empty(E).log_normal_(-6.0, 0.5, generator=g).to(dev)
+    pt_out = torch.empty(R, 2 * N, dtype=torch.bfloat16, device=dev)
+    stages = {
+        "routing (route_hist+scan+scatter)": (
+            lambda: pkg.permute.moe_route_for_gemm(st["topk_ids"], T, E, E, None, 2 * N, K, K, N, tm),
+            R * 4 + (E + 1) * 8 + 2 * R * 4, 0),
+        "permute+quant (quant_rows_kernel gather + scales_to_qf)": (
+            lambda: pkg.quant.fused_permute_quant_int8_hybrid_grouped(
+                st["hidden"], tr["pidx"], k, cfg.quant_block, cfg.q_max, cfg.sg,
+                tr["expert_offsets"], tm, so),
+            T * K * es + R * K + R * 4 + rows_s * (kb1 + sg1) * 4, 0),
+        "w13 GEMM + SiLU*up + requant epilogue": (
+            lambda: pkg.quant.fused_w13_silu_quant_int8_hybrid_grouped(
+                tr["a1q"], tr["a1_Q"], tr["a1_F"], st["w1"], st["w1_qscale"], st["w1_fscale"],
+                tr["expert_offsets"], tr["problem_sizes1"], so, cfg.quant_block, cfg.q_max,
+                cfg.sg, tm, dt),
+            R * K + e_hit * 2 * N * K + R * N + e_hit * (2 * N // 64) * (kb1 + sg1) * 4
+            + rows_s * (kb1 + sg1 + kb2 + sg2) * 4, 2 * R * 2 * N * K),
+        "w13 GEMM, store epilogue (unfused path)": (
+            lambda: gemm(tr["a1q"], tr["a1_Q"], tr["a1_F"], st["w1"], st["w1_qscale"],
+                         st["w1_fscale"], tr["expert_offsets"], tr["problem_sizes1"], mm1,
+                         cfg.quant_block, cfg.sg, tr["a1_so"]),
+            R * K + e_hit * 2 * N * K + R * 2 * N * es + e_hit * (2 * N // 64) * (kb1 + sg1) * 4
+            + rows_s * (kb1 + sg1) * 4, 2 * R * 2 * N * K),
+        "w2 GEMM": (
+            lambda: gemm(tr["a2q"], tr["a2_Q"], tr["a2_F"], st["w2"], st["w2_qscale"],
+                         st["w2_fscale"], tr["expert_offsets"], tr["problem_sizes2"], mm2,
+                         cfg.quant_block, cfg.sg, tr["a2_so"]),
+            R * N + e_hit * K * N + R * K * es + e_hit * (K // 64) * (kb2 + sg2) * 4
+            + rows_s * (kb2 + sg2) * 4, 2 * R * K * N),
+        "unpermute": (
+            lambda: pkg.permute.moe_unpermute(st["output"], mm2, st["topk_weights"], tr["inv"],
+                                              tr["eft"]),
+            R * K * es + T * K * es + T * k * 8, 0),
+        "per-tensor grouped GEMM, w13 shape (per-token x per-expert scales)": (
+            lambda: pkg.ops.int8_grouped_mm_scaled(tr["a1q"], st["w1"], pt_out, row_scale,
+                                                   exp_scale, tr["expert_offsets"],
+                                                   tr["problem_sizes1"]),
+            R * K + e_hit * 2 * N * K + R * 2 * N * 2 + R * 4 + E * 4, 2 * R * 2 * N * K),
+    }
+    res = {}
+    with ClockSampler(local) as clk:
+        t_fwd = _graph_time(fwd)
+        for name, (fn, nbytes, ops) in stages.items():
+            t = _graph_time(fn)
+            d = {"us": t * 1e6, "algorithmic_bytes": nbytes, "gbs": nbytes / t / 1e9,
+                 "frac_hbm": nbytes / t / 1e9 / hbm}
+            if ops:
+                d["int8_tops"] = ops / t / 1e12
+            res[name] = d
+    line = {"breakdown": res, "forward_us": t_fwd * 1e6,
+            "config": {"workload": f"{cfg.name}: T={cfg.T},K={K},N={N},E={E},top{k},{cfg.dtype}",
+                       "tile_m": tm, "experts_with_rows": e_hit},
+            "hbm_peak_gbs": hbm, "peak_source": src, "clocks": clk.summary(),
+            "device_error": pkg._lib.device_error(local)}
+    print(json.dumps(line), flush=True)
+
+
+class PipelinedE2E:
+    """End-to-end steps through a public entry point with host buffers.
+
+    Every step copies its inputs from pinned host memory and reads its output
+    back, all inside the timed region.  The copies run on their own streams
+    with double-buffered device tensors, so step i+1's upload and step i-1's
+    download overlap step i's forward (a serving loop's pipelining); events
+    order each buffer's reuse.  ``fwd(inputs, out)`` runs one forward on the
+    current stream."""
+
+    def __init__(self, fwd, host_inputs, like_inputs, like_out):
+        self.fwd = fwd
+        self.h_in = [t.pin_memory() for t in host_inputs]
+        self.h_out = [torch.empty(like_out.shape, dtype=like_out.dtype).pin_memory()
+                      for _ in range(2)]
+        self.d_in = [[torch.empty_like(t) for t in like_inputs] for _ in range(2)]
+        self.d_out = [torch.empty_like(like_out) for _ in range(2)]
+        self.s_h2d, self.s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        ev = lambda: [torch.cuda.Event() for _ in range(2)]
+        self.in_ready, self.consumed, self.computed, self.downloaded = ev(), ev(), ev(), ev()
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.h_in)
+        self.d2h_bytes = self.h_out[0].numel() * self.h_out[0].element_size()
+
+    def _upload(self, i):
+        b = i % 2
+        with torch.cuda.stream(self.s_h2d):
+            if i >= 2:
+                self.s_h2d.wait_event(self.consumed[b])
+            for dst, src in zip(self.d_in[b], self.h_in):
+                dst.copy_(src, non_blocking=True)
+            self.in_ready[b].record(self.s_h2d)
+
+    def run(self, n):
+        s = torch.cuda.current_stream()
+        start = torch.cuda.Event()
+        start.record(s)
+        self.s_h2d.wait_event(start)
+        self._upload(0)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                self._upload(i + 1)
+            s.wait_event(self.in_ready[b])
+            if i >= 2:
+                s.wait_event(self.downloaded[b])
+            self.fwd(self.d_in[b], self.d_out[b])
+            self.consumed[b].record(s)
+            self.computed[b].record(s)
+            with torch.cuda.stream(self.s_d2h):
+                self.s_d2h.wait_event(self.computed[b])
+                self.h_out[b].copy_(self.d_out[b], non_blocking=True)
+                self.downloaded[b].record(self.s_d2h)
+        s.wait_event(self.downloaded[(n - 1) % 2])
+
+    def last_output(self, n):
+        return self.h_out[(n - 1) % 2]
+
+
 def run_ours_ep(args, world, rank, local):
     """Expert-parallel forward over ``world`` GPUs: the NVLink peer-memory
     exchange with every step a CUDA-graph replay (default), or the NCCL
@@ -419,34 +634,24 @@ def run_ours_ep(args, world, rank, local):
 
     e2e = None
     if not args.no_e2e:
-        h_hidden, h_ids, h_w = (inp["hidden"][sl].pin_memory(), inp["topk_ids"][sl].pin_memory(),
-                                inp["topk_weights"][sl].pin_memory())
-        h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        d_hidden, d_ids, d_w = torch.empty_like(hidden), torch.empty_like(ids), torch.empty_like(wts)
-
-        def e2e_step():
-            d_hidden.copy_(h_hidden, non_blocking=True)
-            d_ids.copy_(h_ids, non_blocking=True)
-            d_w.copy_(h_w, non_blocking=True)
-            moe.forward(d_hidden, d_ids, d_w, out)
-            h_out.copy_(out, non_blocking=True)
-
-        for _ in range(args.warmup):
-            e2e_step()
+        pipe = PipelinedE2E(lambda d_in, o: moe.forward(d_in[0], d_in[1], d_in[2], o),
+                            (inp["hidden"][sl], inp["topk_ids"][sl], inp["topk_weights"][sl]),
+                            (hidden, ids, wts), out)
+        pipe.run(max(args.warmup, 3))
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
         e0.record(s)
-        for _ in range(args.steps):
-            e2e_step()
+        pipe.run(args.steps)
         e1.record(s)
         torch.cuda.synchronize()
         barrier(world)
         dte = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
-        bi = h_hidden.numel() * h_hidden.element_size() + h_ids.numel() * 4 + h_w.numel() * 4
         e2e = {"value": world * ops_per_step * args.steps / dte / 1e12, "unit": "TOPS",
-               "ms_per_step": dte / args.steps * 1e3, "h2d_bytes_per_step": bi,
-               "d2h_bytes_per_step": h_out.numel() * h_out.element_size()}
+               "ms_per_step": dte / args.steps * 1e3, "h2d_bytes_per_step": pipe.h2d_bytes,
+               "d2h_bytes_per_step": pipe.d2h_bytes,
+               "copies": "each step's H2D and D2H inside the timed region, overlapping the "
+                         "neighbouring steps' forwards (double-buffered, separate streams)"}
 
     # roofline: this rank's local w13 GEMM, timed like the single-GPU one
     tr = {}
@@ -542,71 +747,26 @@ def run_ours(args, world, rank, local):
     # ---- end-to-end through the public API with host buffers ----
     e2e = None
     if not args.no_e2e:
-        # Every step copies its inputs from pinned host memory and reads its
-        # output back, all inside the timed region.  The copies run on their
-        # own streams with double-buffered device tensors, so step i+1's
-        # upload and step i-1's download overlap step i's forward (a serving
-        # loop's pipelining); events order each buffer's reuse.
-        h_hidden = inp["hidden"].pin_memory()
-        h_ids = inp["topk_ids"].pin_memory()
-        h_w = inp["topk_weights"].pin_memory()
-        h_out = [torch.empty_like(st["output"], device="cpu").pin_memory() for _ in range(2)]
-        d_in = [(torch.empty_like(st["hidden"]), torch.empty_like(st["topk_ids"]),
-                 torch.empty_like(st["topk_weights"])) for _ in range(2)]
-        d_out = [torch.empty_like(st["output"]) for _ in range(2)]
-        s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
-        ev = lambda: [torch.cuda.Event() for _ in range(2)]
-        in_ready, consumed, computed, downloaded = ev(), ev(), ev(), ev()
-
-        def upload(i):
-            b = i % 2
-            with torch.cuda.stream(s_h2d):
-                if i >= 2:
-                    s_h2d.wait_event(consumed[b])
-                for dst, src in zip(d_in[b], (h_hidden, h_ids, h_w)):
-                    dst.copy_(src, non_blocking=True)
-                in_ready[b].record(s_h2d)
-
-        def run(n):
-            start = torch.cuda.Event()
-            start.record(s)
-            s_h2d.wait_event(start)
-            upload(0)
-            for i in range(n):
-                b = i % 2
-                if i + 1 < n:
-                    upload(i + 1)
-                s.wait_event(in_ready[b])
-                if i >= 2:
-                    s.wait_event(downloaded[b])
-                fwd(hidden=d_in[b][0], topk_ids=d_in[b][1], topk_weights=d_in[b][2],
-                    output=d_out[b])
-                consumed[b].record(s)
-                computed[b].record(s)
-                with torch.cuda.stream(s_d2h):
-                    s_d2h.wait_event(computed[b])
-                    h_out[b].copy_(d_out[b], non_blocking=True)
-                    downloaded[b].record(s_d2h)
-            s.wait_event(downloaded[(n - 1) % 2])
-
-        run(max(args.warmup, 3))
+        pipe = PipelinedE2E(
+            lambda d_in, o: fwd(hidden=d_in[0], topk_ids=d_in[1], topk_weights=d_in[2], output=o),
+            (inp["hidden"], inp["topk_ids"], inp["topk_weights"]),
+            (st["hidden"], st["topk_ids"], st["topk_weights"]), st["output"])
+        pipe.run(max(args.warmup, 3))
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
         e0.record(s)
-        run(args.steps)
+        pipe.run(args.steps)
         e1.record(s)
         torch.cuda.synchronize()
         barrier(world)
         dte = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
-        bi = h_hidden.numel() * h_hidden.element_size() + h_ids.numel() * 4 + h_w.numel() * 4
-        bo = h_out[0].numel() * h_out[0].element_size()
         graph.replay()  # the device-timed forward of the same inputs, for a check
         torch.cuda.synchronize()
-        same = torch.equal(h_out[(args.steps - 1) % 2], st["output"].cpu())
+        same = torch.equal(pipe.last_output(args.steps), st["output"].cpu())
         e2e = {"value": world * ops_per_step * args.steps / dte / 1e12, "unit": "TOPS",
-               "ms_per_step": dte / args.steps * 1e3, "h2d_bytes_per_step": bi,
-               "d2h_bytes_per_step": bo,
+               "ms_per_step": dte / args.steps * 1e3, "h2d_bytes_per_step": pipe.h2d_bytes,
+               "d2h_bytes_per_step": pipe.d2h_bytes,
                "copies": "each step's H2D and D2H inside the timed region, overlapping the "
                          "neighbouring steps' forwards (double-buffered, separate streams)",
                "output_matches_device_run": same}
@@ -665,6 +825,16 @@ def run_ours(args, world, rank, local):
 def main():
     args = parse_args()
     world, rank, local = dist_setup(args)
+    if args.breakdown:
+        if world == 1:
+            run_breakdown(args, local)
+        return
+    if args.int8_peak:
+        if rank == 0:
+            print(json.dumps({"int8_mma_peak": int8_mma_peak(local)}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)

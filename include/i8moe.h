@@ -299,6 +299,15 @@ int i8moe_int8_grouped_mm(const int8_t* a, const int8_t* b, void* out, int out_d
  * I8MOE_ERR_INVALID for another value. */
 int i8moe_gemm_set_cta_pairs(int mode);
 
+/* No reference counterpart: the measured dense INT8 tensor-core peak.
+ * Launches one CTA per SM (cta_group 1) or one CTA pair per two SMs
+ * (cta_group 2, M = 256), each issuing `steps` x 4 tcgen05.mma kind::i8
+ * (M x 256 x 32) back to back from shared memory into TMEM, nothing else.
+ * The caller times the launch on `stream`; each CTA performs
+ * 2 * 128 * 256 * 128 * steps int8 operations, and *n_cta receives the
+ * number of CTAs launched.  The denominator of the INT8 roofline fractions. */
+int i8moe_int8_mma_peak(int64_t steps, int cta_group, int64_t* n_cta, i8moe_stream_t stream);
+
 /* ---------------------------------------------------- expert parallelism */
 /* No reference counterpart: the device-side bookkeeping of the expert-
  * parallel dispatch and combine (the all-to-alls themselves are NCCL calls

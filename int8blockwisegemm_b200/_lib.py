@@ -65,6 +65,7 @@ PROTOTYPES = {
                                                    P, P]),
     "i8moe_int8_grouped_mm": (I32, [P, P, P, I32, c_float, P, P, P, P, I64, I64, I64, I64, P]),
     "i8moe_gemm_set_cta_pairs": (I32, [I32]),
+    "i8moe_int8_mma_peak": (I32, [I64, I32, P, P]),
 }
 
 BF16, FP16, FP32, S32 = 0, 1, 2, 3

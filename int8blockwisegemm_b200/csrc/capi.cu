@@ -49,6 +49,7 @@ int read_route_error(uint32_t* w, int clear);
 int read_quant_error(uint32_t* w, int clear);
 int read_gemm_error(uint32_t* w, int clear);
 int read_ep_error(uint32_t* w, int clear);
+int read_peak_error(uint32_t* w, int clear);
 
 }  // namespace i8moe
 
@@ -67,10 +68,11 @@ int i8moe_device_error(int device, uint32_t* word, int clear) {
   int rc = i8moe::read_route_error(&a, clear);
   if (rc == I8MOE_OK) rc = i8moe::read_quant_error(&b, clear);
   if (rc == I8MOE_OK) rc = i8moe::read_gemm_error(&c, clear);
-  uint32_t d = 0;
+  uint32_t d = 0, e = 0;
   if (rc == I8MOE_OK) rc = i8moe::read_ep_error(&d, clear);
+  if (rc == I8MOE_OK) rc = i8moe::read_peak_error(&e, clear);
   cudaSetDevice(prev);
-  if (word) *word = a | b | c | d;
+  if (word) *word = a | b | c | d | e;
   return rc;
 }
 

@@ -714,7 +714,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool lead = cq == 0 && quad == (p.tile_m == 64 ? 2 * grp : 0) && lane == 0;
         if (lead) red[(lt + 2) % 3] = 0u;
         const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 127.0f);
-        const float inv = __frcp_rn(scale);
+        const QuantInv qi = quant_inv(scale);
         const int grow0 = ti.mt * BM + (p.tile_m == 64 ? 64 * grp : 0);
         if (lead && grow0 < m_e) {
           const int srow = so_prefix[ti.e] + grow0 / p.tile_m;
@@ -723,10 +723,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t qw[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          uint32_t w2[2];
-          if (!quant_chunk_fast<OutT>(act[j], inv, w2)) quant_chunk_exact<OutT>(act[j], inv, scale, w2);
-          qw[2 * j] = w2[0];
-          qw[2 * j + 1] = w2[1];
+          uint2 q2;
+          if (!quant_chunk_bracket<OutT>(act[j], qi, q2)) q2 = quant_chunk_exact16<OutT>(act[j], scale);
+          qw[2 * j] = q2.x;
+          qw[2 * j + 1] = q2.y;
         }
         if (wrow0 + 32 <= m_e && col0 + 32 <= p.n_act) {
           // whole warp inside the expert: 32 rows x 32 bytes staged with the

@@ -158,8 +158,15 @@ __global__ void __launch_bounds__(kQuantThreads, (RowsTile<T, TM, MODE>::MIN_BLO
     }
     // ---- tile absmax (NaN-ignoring, as tl.max / fmaxf) ----
     float m = 0.0f;
+    if constexpr (sizeof(T) == 2) {
+      uint32_t acc = 0u;
 #pragma unroll
-    for (int j = 0; j < NP; ++j) m = fmaxf(m, chunk_absmax<T>(v[j]));
+      for (int j = 0; j < NP; ++j) acc = absmax16_acc<T>(acc, v[j]);
+      m = absmax16_value<T>(acc);
+    } else {
+#pragma unroll
+      for (int j = 0; j < NP; ++j) m = fmaxf(m, chunk_absmax<T>(v[j]));
+    }
     const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
     const int buf = (kb - kb0) & 1;  // alternate, so one barrier per K-block suffices
     if (lane == 0) s_red[buf][warp] = __uint_as_float(mb);
@@ -168,25 +175,37 @@ __global__ void __launch_bounds__(kQuantThreads, (RowsTile<T, TM, MODE>::MIN_BLO
 #pragma unroll
     for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, s_red[buf][w]);
     const float scale = __fdiv_rn(fmaxf(amax, 1e-10f), 127.0f);
-    const float inv = __frcp_rn(scale);
     if (tid == 0) a.scale_out[static_cast<int64_t>(s) * a.Kb + kb] = scale;
     // ---- quantise and store ----
     if (!col_ok) continue;
+    if constexpr (sizeof(T) == 2) {
+      const QuantInv qi = quant_inv(scale);
 #pragma unroll
-    for (int j = 0; j < NP; ++j) {
-      const int r = j * RPP + warp * RPW + lane / CPR;
-      if (r >= rows) continue;
-      uint32_t words[EPC / 4];
-      if (!quant_chunk_fast<T>(v[j], inv, words)) quant_chunk_exact<T>(v[j], inv, scale, words);
-      if (static_cast<unsigned>(row_start + r) >= static_cast<unsigned>(a.M)) {
-        atomicOr(&g_err_quant, kErrBadIndex);  // never store outside qA
-        continue;
+      for (int j = 0; j < NP; ++j) {
+        const int r = j * RPP + warp * RPW + lane / CPR;
+        if (r >= rows) continue;
+        uint2 q;
+        if (!quant_chunk_bracket<T>(v[j], qi, q)) q = quant_chunk_exact16<T>(v[j], scale);
+        if (static_cast<unsigned>(row_start + r) >= static_cast<unsigned>(a.M)) {
+          atomicOr(&g_err_quant, kErrBadIndex);  // never store outside qA
+          continue;
+        }
+        *reinterpret_cast<uint2*>(a.qA + static_cast<int64_t>(row_start + r) * a.K + col) = q;
       }
-      int8_t* dst = a.qA + static_cast<int64_t>(row_start + r) * a.K + col;
-      if constexpr (EPC == 8) {
-        *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[1]);
-      } else {
-        *reinterpret_cast<uint32_t*>(dst) = words[0];
+    } else {
+      const float inv = __frcp_rn(scale);
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        const int r = j * RPP + warp * RPW + lane / CPR;
+        if (r >= rows) continue;
+        uint32_t words[EPC / 4];
+        if (!quant_chunk_fast<T>(v[j], inv, words)) quant_chunk_exact<T>(v[j], inv, scale, words);
+        if (static_cast<unsigned>(row_start + r) >= static_cast<unsigned>(a.M)) {
+          atomicOr(&g_err_quant, kErrBadIndex);  // never store outside qA
+          continue;
+        }
+        *reinterpret_cast<uint32_t*>(a.qA + static_cast<int64_t>(row_start + r) * a.K + col) =
+            words[0];
       }
     }
   }

@@ -155,6 +155,117 @@ __device__ __forceinline__ bool quant_chunk_fast(const uint4& v, float inv,
   return dmax < 0.49997f;
 }
 
+// ---------------------------------------------------------------------------
+// Bracketed INT8 quantisation of 16-bit chunks.
+//
+// With inv = RN(1/scale), inv_lo = RD(inv * (1 - 2^-20)) and
+// inv_hi = RU(inv * (1 + 2^-20)), the IEEE quotient RN(x / scale) lies
+// strictly between x * inv_lo and x * inv_hi (the reciprocal and the
+// quotient are each within 2^-24 relative of exact, far inside the 2^-20
+// margin).  Both products are rounded to an integer by one FMA each
+// (fma(x, inv, 1.5 * 2^23): round to nearest even, the integer in the low
+// bits of the result).  Rounding is monotonic, so when the two integers agree
+// every value between them -- the quotient included -- rounds to that integer,
+// and the quotient is not an exact tie (a tie k + 0.5 strictly inside the
+// bracket would round the ends to k and k + 1), so round-half-away equals
+// round-to-nearest-even there.  Agreement is tested for a whole chunk at once:
+// s += (t_lo - t_hi)^2 stays 0 exactly when every pair agrees and no value is
+// NaN or infinite; otherwise the chunk is recomputed with the IEEE division.
+// |x / scale| <= 127 (1 + 2^-23) because |x| <= the tile absmax, so no clamp
+// binds on the fast path.  Packed f32x2 arithmetic throughout.
+// ---------------------------------------------------------------------------
+struct QuantInv {
+  float lo, hi;
+};
+
+__device__ __forceinline__ QuantInv quant_inv(float scale) {
+  const float inv = __frcp_rn(scale);
+  return QuantInv{__fmul_rd(inv, 1.0f - 0x1p-20f), __fmul_ru(inv, 1.0f + 0x1p-20f)};
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// two 16-bit values of one word -> their float32 values as an f32x2 pair
+template <typename T>
+__device__ __forceinline__ uint64_t f2_from16(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return (static_cast<uint64_t>(w & 0xFFFF0000u) << 32) | static_cast<uint32_t>(w << 16);
+  } else {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w);
+    const float2 f = __half22float2(h);
+    return f2_pack(f.x, f.y);
+  }
+}
+
+// Fast path for one 8-element chunk of bf16 / fp16: the eight int8 values in
+// out; false if the chunk needs the exact path.
+template <typename T>
+__device__ __forceinline__ bool quant_chunk_bracket(const uint4& v, const QuantInv& qi,
+                                                    uint2& out) {
+  static_assert(sizeof(T) == 2, "16-bit activations");
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t lo2 = f2_pack(qi.lo, qi.lo), hi2 = f2_pack(qi.hi, qi.hi);
+  const uint64_t m2 = f2_pack(kMagic, kMagic);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t b[4];
+  uint64_t s = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t x = f2_from16<T>(w[i]);
+    const uint64_t ta = f2_fma(x, lo2, m2);
+    const uint64_t tb = f2_fma(x, hi2, m2);
+    const uint64_t d = f2_sub(ta, tb);
+    s = f2_fma(d, d, s);
+    // low byte of each lane's integer, lanes 0 and 1 in bytes 0 and 1
+    b[i] = __byte_perm(static_cast<uint32_t>(ta), static_cast<uint32_t>(ta >> 32), 0x0040);
+  }
+  out.x = __byte_perm(b[0], b[1], 0x5410);
+  out.y = __byte_perm(b[2], b[3], 0x5410);
+  return (static_cast<uint32_t>(s) | static_cast<uint32_t>(s >> 32)) == 0u;
+}
+
+// Exact reference rounding of one 8-element 16-bit chunk, returned by value.
+template <typename T>
+__device__ __noinline__ uint2 quant_chunk_exact16(uint4 v, float scale) {
+  uint32_t q[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    q[i] = static_cast<uint8_t>(quant_exact(Num<T>::to_f(reinterpret_cast<const T*>(&v)[i]), scale));
+  return make_uint2(q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24),
+                    q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24));
+}
+
+// Running |x|-max of 16-bit chunks as a packed pair (NaN-ignoring, as fmaxf):
+// acc starts at 0; absmax16_value gives the float maximum.
+template <typename T>
+__device__ __forceinline__ uint32_t absmax16_acc(uint32_t acc, const uint4& v) {
+  uint32_t r = acc;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+      asm("max.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(r) : "r"(w[i]));
+    else
+      asm("max.xorsign.abs.f16x2 %0, %0, %1;" : "+r"(r) : "r"(w[i]));
+  }
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ float absmax16_value(uint32_t acc) {
+  acc &= 0x7FFF7FFFu;  // the xorsign form leaves a sign bit
+  const T* h = reinterpret_cast<const T*>(&acc);
+  return fmaxf(Num<T>::to_f(h[0]), Num<T>::to_f(h[1]));
+}
+
 // Exact reference rounding for one chunk: round_half_away(clamp(x / scale)).
 template <typename T>
 __device__ __noinline__ void quant_chunk_exact(uint4 v, float inv, float scale,

@@ -23,14 +23,18 @@ all-to-all:
   and round once.  Only this summation order differs from one GPU, so the
   output agrees within the reference's tolerance rather than bit for bit.
 
-The all-to-alls are ``torch.distributed.all_to_all_single`` calls (NCCL over
-NVLink/NVSwitch on GPUs; gloo for the CPU tests).  On GPUs the bookkeeping
-around them runs in the library's kernels (csrc/ep.cu): a plan kernel gives
-every token its slot in each destination's segment, a pack kernel gathers the
-rows with their top-k ids and weights, and a combine kernel sums the returned
-partial rows.  The segment lengths of all ranks travel first (one all-gather)
-and their host copy sizes the payload exchange: one host synchronisation per
-dispatch.  Tensors on the CPU take an equivalent torch-only path.
+Two exchanges implement that on GPUs.  ``PeerExchange`` (the default of
+``bench.py``) stores rows straight into the peers' receive buffers over NVLink
+peer memory with device-side flags: no NCCL call and no host synchronisation
+per step, so whole steps are CUDA-graph replays.  ``ExpertParallel`` uses
+NCCL ``all_to_all_single`` calls; the bookkeeping around them runs in the
+library's kernels (csrc/ep.cu): a plan kernel gives every token its slot in
+each destination's segment, a pack kernel gathers the rows with their top-k
+ids and weights, and a combine kernel sums the returned partial rows.  The
+segment lengths of all ranks travel first (one all-gather) and their host copy
+sizes the payload exchange: one host synchronisation per dispatch.  There is
+no CPU path; the gloo tests run the same exchange order with a torch-only
+stand-in kept under tests/.
 """
 
 from __future__ import annotations
@@ -83,32 +87,10 @@ class ExpertParallel:
 
     def dispatch(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
                  topk_weights: torch.Tensor) -> Dispatched:
-        if hidden.is_cuda:
-            return self._dispatch_cuda(hidden, topk_ids, topk_weights)
-        T, k = topk_ids.shape
-        dev = hidden.device
-        dest = topk_ids.long() // self.n_local                       # [T, k]
-        member = torch.zeros(T, self.world, dtype=torch.bool, device=dev)
-        member.scatter_(1, dest.clamp(0, self.world - 1), True)
-        # rows for rank d: the tokens with an expert on d, in token order
-        order = member.t().nonzero()                                 # [n_send, 2] (rank, token)
-        send_idx = order[:, 1]
-        counts = member.sum(0).to(torch.int64)                       # [P]
-        recv = torch.empty_like(counts)
-        self._a2a(recv, counts, [1] * self.world, [1] * self.world)
-        send_counts = counts.cpu().tolist()
-        recv_counts = recv.cpu().tolist()
-        n_recv = sum(recv_counts)
-        r_hidden = torch.empty(n_recv, hidden.shape[1], dtype=hidden.dtype, device=dev)
-        r_ids = torch.empty(n_recv, k, dtype=torch.int32, device=dev)
-        r_w = torch.empty(n_recv, k, dtype=torch.float32, device=dev)
-        self._a2a(r_hidden, hidden.index_select(0, send_idx).contiguous(), recv_counts,
-                  send_counts)
-        self._a2a(r_ids, topk_ids.to(torch.int32).index_select(0, send_idx).contiguous(),
-                  recv_counts, send_counts)
-        self._a2a(r_w, topk_weights.to(torch.float32).index_select(0, send_idx).contiguous(),
-                  recv_counts, send_counts)
-        return Dispatched(r_hidden, r_ids, r_w, send_idx, send_counts, recv_counts, T)
+        if not hidden.is_cuda:
+            raise RuntimeError("expert parallelism runs on CUDA tensors (sm_100a); "
+                               "there is no CPU path")
+        return self._dispatch_cuda(hidden, topk_ids, topk_weights)
 
     def _dispatch_cuda(self, hidden, topk_ids, topk_weights) -> Dispatched:
         from ._lib import call
@@ -149,21 +131,10 @@ class ExpertParallel:
     def combine(self, d: Dispatched, partial: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         """Return the partial rows to their sources and sum them per token."""
-        if partial.is_cuda and d.pos is not None:
-            return self._combine_cuda(d, partial, out)
-        K = partial.shape[1]
-        back = torch.empty(sum(d.send_counts), K, dtype=partial.dtype, device=partial.device)
-        self._a2a(back, partial.contiguous(), d.send_counts, d.recv_counts)
-        acc = torch.zeros(d.n_token, K, dtype=torch.float32, device=partial.device)
-        start = 0
-        for n in d.send_counts:  # each segment holds distinct tokens: a deterministic order
-            if n:
-                acc.index_add_(0, d.send_idx[start:start + n], back[start:start + n].float())
-            start += n
-        if out is None:
-            return acc.to(partial.dtype)
-        out.copy_(acc)
-        return out
+        if not (partial.is_cuda and d.pos is not None):
+            raise RuntimeError("expert parallelism runs on CUDA tensors (sm_100a); "
+                               "there is no CPU path")
+        return self._combine_cuda(d, partial, out)
 
     def _combine_cuda(self, d: Dispatched, partial: torch.Tensor, out):
         from ._lib import BF16, FP16, call

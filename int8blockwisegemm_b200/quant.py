@@ -1,8 +1,9 @@
 """Activation quantisation entry points with the reference's signatures and
 return values (int8_hybrid_moe/quant.py:99-140, 212-277, 360-433, 514-579),
-computed by the sm_100a cluster kernels of libi8moe (csrc/quant.cu): the
-per-(expert M-tile x 128-K block) absmax INT8 quantisation and the two-level
-(Q int32, F fp32) scale factorisation run in one launch.
+computed by the sm_100a kernels of libi8moe (csrc/quant.cu): two launches,
+``quant_rows_kernel`` (the per-(expert M-tile x 128-K block) absmax INT8
+quantisation, writing the raw block scales into the Q buffer) and
+``scales_to_qf`` (the two-level Q int32 / F fp32 factorisation, in place).
 
 Each function returns ``(qA, Q_A, F_A, scale_offsets_i32)`` with
 Q_A [cdiv(M, tile_m) + E, K_blocks] and F_A [same rows, num_super_groups];

@@ -1,4 +1,5 @@
-"""Expert-parallel dispatch / combine on CPU: two gloo ranks, the numpy oracle
+"""Expert-parallel dispatch / combine on CPU (the torch-only stand-in of
+tests/ep_cpu_exchange.py): gloo ranks, the numpy oracle
 as each rank's local forward, checked against one single-process oracle
 forward of all tokens.  Per expert the INT8 activations, mm1 and a2q rows
 are bit-identical; the combined output is within the reference tolerance
@@ -32,7 +33,7 @@ def _worker(rank, world, port, cfg_name, only_rank0_experts, errq):
         import torch.distributed as dist
         from oracle import ref_cpu as ref
         from tests.helpers import load_workloads
-        from int8blockwisegemm_b200.ep import ExpertParallel
+        from tests.ep_cpu_exchange import CPUExchange
 
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -46,7 +47,7 @@ def _worker(rank, world, port, cfg_name, only_rank0_experts, errq):
             ids = ids % (cfg.E // world)
         T, k = ids.shape
         tm = ref.VARIANT_TILE_M[ref.pick_grouped_hybrid_variant(T * k, cfg.E)]
-        ep = ExpertParallel(cfg.E)
+        ep = CPUExchange(cfg.E)
         lo, n = ep.first, ep.n_local
         per = T // world
         sl = slice(rank * per, (rank + 1) * per)
