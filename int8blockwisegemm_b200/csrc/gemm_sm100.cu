@@ -146,6 +146,13 @@ struct SmemLayout {
   static constexpr int bytes(int E) { return kPrefix + 4 * (E + 1) * 4 + 32; }
 };
 
+// The _bias epilogue as the reference evaluates it: the scaled accumulator
+// rounded to fp32 first, then the bias added (a separate rounding, no FMA;
+// int8_hybrid_grouped_gemm.cu:449-458 -- pinned by running the reference).
+__device__ __forceinline__ float bias_epi(int32_t w, float f, float bias) {
+  return __fadd_rn(__fmul_rn(static_cast<float>(w), f), bias);
+}
+
 template <typename OutT>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -672,11 +679,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) {
             const int c = 8 * j + 2 * i;
             if (HAS_BIAS) {
-              g4[i] = pack2<OutT>(fmaf(static_cast<float>(W[c]), fg, __ldg(bg + c)),
-                                  fmaf(static_cast<float>(W[c + 1]), fg, __ldg(bg + c + 1)));
-              u4[i] = pack2<OutT>(
-                  fmaf(static_cast<float>(W[32 + c]), fu, __ldg(bg + p.n_act + c)),
-                  fmaf(static_cast<float>(W[32 + c + 1]), fu, __ldg(bg + p.n_act + c + 1)));
+              g4[i] = pack2<OutT>(bias_epi(W[c], fg, __ldg(bg + c)),
+                                  bias_epi(W[c + 1], fg, __ldg(bg + c + 1)));
+              u4[i] = pack2<OutT>(bias_epi(W[32 + c], fu, __ldg(bg + p.n_act + c)),
+                                  bias_epi(W[32 + c + 1], fu, __ldg(bg + p.n_act + c + 1)));
             } else {
               g4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[c]), fg),
                                   __fmul_rn(static_cast<float>(W[c + 1]), fg));
@@ -788,8 +794,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 4; ++i) {
                 const int c = 32 * h + 8 * j + 2 * i;
                 if (HAS_BIAS) {
-                  w4[i] = pack2<OutT>(fmaf(static_cast<float>(W[c]), f, __ldg(bp + c)),
-                                      fmaf(static_cast<float>(W[c + 1]), f, __ldg(bp + c + 1)));
+                  w4[i] = pack2<OutT>(bias_epi(W[c], f, __ldg(bp + c)),
+                                      bias_epi(W[c + 1], f, __ldg(bp + c + 1)));
                 } else {
                   w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[c]), f),
                                       __fmul_rn(static_cast<float>(W[c + 1]), f));
@@ -834,8 +840,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) {
             const int j = 8 * c + 2 * i;
             if (HAS_BIAS) {
-              w4[i] = pack2<OutT>(fmaf(static_cast<float>(W[j]), f, __ldg(bp + j)),
-                                  fmaf(static_cast<float>(W[j + 1]), f, __ldg(bp + j + 1)));
+              w4[i] = pack2<OutT>(bias_epi(W[j], f, __ldg(bp + j)),
+                                  bias_epi(W[j + 1], f, __ldg(bp + j + 1)));
             } else {
               w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[j]), f),
                                   __fmul_rn(static_cast<float>(W[j + 1]), f));

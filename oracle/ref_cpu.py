@@ -401,7 +401,7 @@ def hybrid_grouped_gemm(A, QA, FA, B, QB, FB, expert_offsets, problem_sizes,
       P_qb  = sum_{k in q-block qb} A[r,k] * B[e,n,k]                  (:344-432)
       W     = sum_qb (QA[s,qb] * QB[e,j,qb]) * P_qb    int32, wrapping (:433-442)
       out   = dtype_rn(float(W) * (FA[s,0] * FB[e,j,0]))               (:445-453,472-475)
-      (_bias variants: fma(float(W), F, bias[n]) before rounding, :455-458)
+      (_bias variants: float32(float(W) * F) + bias[n], two roundings, :449-458)
     Only the first super-group's F is read (:445-447).
 
     ``out`` rows that belong to no expert are left untouched.  With
@@ -457,7 +457,7 @@ def hybrid_grouped_gemm(A, QA, FA, B, QB, FB, expert_offsets, problem_sizes,
         else:
             bias = np.asarray(bias, np.float32)
             bvec = bias[e] if bias.ndim == 2 else bias
-            y = fma_f32(W.astype(np.float32), f, bvec[None, :])
+            y = (W.astype(np.float32) * f).astype(np.float32) + bvec[None, :].astype(np.float32)
         out[r0:r0 + m_e] = round_to(y, out_dtype)
         if return_w:
             W_all[r0:r0 + m_e] = W

@@ -587,7 +587,7 @@ def test_large_config_stagewise(m, cname):
     np.testing.assert_array_equal(npf(tr["inv"]), o_inv.reshape(-1))
     tm = tr["tile_m"]
     assert tm == 128
-    so = npf(tr["a1_so"]).astype(np.int64)
+    so = npf(tr["scale_offsets"]).astype(np.int64)  # [E+1]
     hidden = npf(inp["hidden"])
     counts = eft[1:] - eft[:-1]
     live = np.nonzero(counts > 0)[0]
