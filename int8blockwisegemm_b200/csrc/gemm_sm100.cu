@@ -11,7 +11,7 @@
 //     out = dtype(float(sum_k a*b) * alpha) with alpha per tensor, or
 //     per-token x per-expert (extension).
 //
-// Structure (one CTA per SM, 18 warps; tiles of 128 rows x 256 columns):
+// Structure (one CTA per SM, 20 warps; tiles of 128 rows x 256 columns):
 //   warp 0      TMA producer: A tile [128 rows x 128 K] and B tile
 //               [BN x 128 K] per K-tile, 128-byte swizzle, into a STAGES-deep
 //               shared-memory ring guarded by full/empty mbarriers.
@@ -21,8 +21,10 @@
 //               accumulator buffers (256 columns each); tcgen05.commit frees
 //               the smem stage and, at the end of a quant block, signals the
 //               epilogue.
-//   warps 2..17 epilogue: TMEM lane quadrant = warp % 4, column quarter =
-//               (warp - 2) / 4.  Each thread owns one output row and 64
+//   warps 2, 3  idle (they complete warpgroup 0, which hands its registers
+//               to the epilogue: setmaxnreg 32 there, 112 in the epilogue)
+//   warps 4..19 epilogue: TMEM lane quadrant = warp % 4, column quarter =
+//               (warp - 4) / 4.  Each thread owns one output row and 64
 //               columns: tcgen05.ld the block partial in 16-column chunks
 //               (other warps' accumulation covers each load's latency),
 //               release the TMEM buffer, W += q * P (int32 IMAD); after the
@@ -72,7 +74,16 @@ constexpr int BN = 256;
 constexpr int BK = 128;  // bytes == int8 elements per K-tile
 constexpr int NACC = 2;
 constexpr int kEpiWarps = 16;
-constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue warps
+// Warps 0-3 (one warpgroup): TMA producer, MMA issuer, two idle; warps 4-19:
+// epilogue.  Launched at kRegsLaunch registers a thread, the first
+// warpgroup gives registers back (setmaxnreg.dec to kRegsLow) and the four
+// epilogue warpgroups take them (setmaxnreg.inc to kRegsHigh):
+// 20 warps x 32 x 96 = 128 x 32 + 512 x 112 registers exactly.
+constexpr int kEpiW0 = 4;
+constexpr int kThreads = 32 * kEpiW0 + 32 * kEpiWarps;  // 640
+constexpr int kRegsLaunch = 96, kRegsLow = 32, kRegsHigh = 112;
+static_assert(kThreads * kRegsLaunch == 32 * kEpiW0 * kRegsLow + 32 * kEpiWarps * kRegsHigh,
+              "register split must use exactly the registers the block is launched with");
 constexpr int kMaxExperts = 1024;
 constexpr int kTileABytes = BM * BK;
 constexpr uint32_t kTmemCols = NACC * BN;
@@ -323,6 +334,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t full0 = CG == 2 ? mapa_shared(bar_full, 0) : bar_full;
   const uint32_t acce0 = CG == 2 ? mapa_shared(bar_acce, 0) : bar_acce;
 
+  if (warp < kEpiW0) {
+  // register split, first warpgroup: gives registers back (the host checked
+  // the launch count); each role's code sits inside its warpgroup's branch
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
   if (warp == 0) {
     // ================= TMA producer =================
     if (lane == 0) {
@@ -480,10 +495,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
+  }
   } else {
+    // register split, epilogue warpgroups: take the registers given back
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ================= epilogue (16 warps) =================
     // TMEM lane quadrant = warp % 4 (hardware rule), column group cq =
-    // (warp - 2) / 4.  Each thread owns one row and 64 accumulator columns:
+    // (warp - kEpiW0) / 4.  Each thread owns one row and 64 accumulator columns:
     //   kEpiStore:      tile columns [64cq, 64cq+64), one 64-column weight-
     //                   scale block, so one Q_A * Q_B factor per quant block;
     //   kEpiSiluQuant:  gate columns [32cq, +32) and the matching up columns
@@ -491,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Four warps share each SM sub-partition, which keeps the integer
     // multiply-add pipe busy while the other warps wait for their TMEM loads.
     const int quad = warp & 3;
-    const int cq = (warp - 2) >> 2;
+    const int cq = (warp - kEpiW0) >> 2;
     const uint32_t t_lane = static_cast<uint32_t>(quad * 32) << 16;
     constexpr bool kFused = EPI == kEpiSiluQuant;
     auto chunk_col = [&](int c) -> uint32_t {  // TMEM column of 16-column chunk c
@@ -516,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Slots: [Q_A, Q_B, Q_B(up)] for even local tiles, the same for odd
     // ones, then F_A, F_B, F_B(up); a slot set is refilled only for the tile
     // after next, so an asynchronous write never meets a pending read.
-    const uint32_t s_slot = sbase + SmemLayout::kSlots + 4 * (threadIdx.x - 64);
+    const uint32_t s_slot = sbase + SmemLayout::kSlots + 4 * (threadIdx.x - 32 * kEpiW0);
     constexpr uint32_t kSA = SmemLayout::kSlotArray;
     const uint32_t s_fa = s_slot + 6 * kSA;
     const uint32_t s_fb = s_slot + 7 * kSA;
@@ -602,9 +620,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 64; ++i) W[i] = 0;
       // One 16-column chunk in flight per warp: with four epilogue warps on
       // each SM sub-partition the other warps' multiply-adds cover the TMEM
-      // load latency, and the single buffer keeps W[64] in registers.  The
-      // accumulator buffer goes back to the MMA warp as soon as its last
-      // chunk has landed.
+      // load latency (two chunks in flight measured slower: the second
+      // buffer's registers cost spills).  The accumulator buffer goes back to
+      // the MMA warp as soon as its last chunk has landed.
       uint32_t P[16];
       for (int qb = 0; qb < p.nq && ok; ++qb) {
         const int q = __shfl_sync(0xffffffffu, qv, qb & 31);
@@ -737,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (wrow0 + 32 <= m_e && col0 + 32 <= p.n_act) {
           // whole warp inside the expert: 32 rows x 32 bytes staged with the
           // 32-byte swizzle, one TMA tensor store
-          const uint32_t stg = sbase + SmemLayout::kStg + (warp - 2) * SmemLayout::kStgWarpBytes;
+          const uint32_t stg = sbase + SmemLayout::kStg + (warp - kEpiW0) * SmemLayout::kStgWarpBytes;
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
 #pragma unroll
@@ -780,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // in shared memory (64-byte swizzle, conflict-free) and write it
           // with two TMA tensor stores of 32 x 32, so the stores leave as
           // whole lines instead of 32 row fragments per instruction.
-          const uint32_t stg = sbase + SmemLayout::kStg + (warp - 2) * SmemLayout::kStgWarpBytes;
+          const uint32_t stg = sbase + SmemLayout::kStg + (warp - kEpiW0) * SmemLayout::kStgWarpBytes;
           const float* bp =
               HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0 : nullptr;
 #pragma unroll
@@ -964,6 +982,13 @@ int launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   const bool cached = dev >= 0 && dev < 64 && __atomic_load_n(&attr_done[dev], __ATOMIC_ACQUIRE);
   int n_pairs = 0;
   if (!cached) {
+    // the register split is exact: any other launch count would leave the
+    // epilogue's setmaxnreg.inc waiting (fewer) or fail to launch (more)
+    cudaFuncAttributes fa;
+    I8_CUDA(cudaFuncGetAttributes(&fa, kern));
+    I8_REQUIRE(fa.numRegs == kRegsLaunch,
+               "grouped GEMM: compiled with %d registers a thread; its register split needs %d",
+               fa.numRegs, kRegsLaunch);
     I8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
     if (CG == 2) {
       cudaLaunchConfig_t q = {};
