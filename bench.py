@@ -85,6 +85,28 @@ def parse_args():
     return ap.parse_args()
 
 
+def int8_peak_tops(steps: int = 20000, reps: int = 3) -> float:
+    """The device's dense INT8 tcgen05 peak (one CTA per SM issuing MMAs
+    from shared memory, i8moe_int8_mma_peak), best of ``reps`` launches, in
+    TOPS: the measured denominator of the INT8 fractions in the JSON line."""
+    import ctypes
+    from int8blockwisegemm_b200 import _lib
+    s = torch.cuda.current_stream()
+    n_cta = ctypes.c_int64(0)
+    _lib.call("i8moe_int8_mma_peak", steps, 1, ctypes.addressof(n_cta), s.cuda_stream)
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        _lib.call("i8moe_int8_mma_peak", steps, 1, ctypes.addressof(n_cta), s.cuda_stream)
+        e1.record(s)
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e-3
+        best = t if best is None else min(best, t)
+    return 2 * 128 * 256 * 128 * steps * n_cta.value / best / 1e12
+
+
 def int8_mma_peak(local: int, steps: int = 40000, reps: int = 5) -> dict:
     """Dense INT8 tensor-core peak: i8moe_int8_mma_peak timed with CUDA
     events (best of ``reps`` launches after one warm-up), with the SM clock
@@ -481,6 +503,7 @@ def run_breakdown(args, local):
             R * K + e_hit * 2 * N * K + R * 2 * N * 2 + R * 4 + E * 4, 2 * R * 2 * N * K),
     }
     res = {}
+    peak_i8 = int8_peak_tops()
     with ClockSampler(local) as clk:
         t_fwd = _graph_time(fwd)
         for name, (fn, nbytes, ops) in stages.items():
@@ -489,11 +512,13 @@ def run_breakdown(args, local):
                  "frac_hbm": nbytes / t / 1e9 / hbm}
             if ops:
                 d["int8_tops"] = ops / t / 1e12
+                d["int8_frac"] = ops / t / 1e12 / peak_i8
             res[name] = d
     line = {"breakdown": res, "forward_us": t_fwd * 1e6,
             "config": {"workload": f"{cfg.name}: T={cfg.T},K={K},N={N},E={E},top{k},{cfg.dtype}",
                        "tile_m": tm, "experts_with_rows": e_hit},
-            "hbm_peak_gbs": hbm, "peak_source": src, "clocks": clk.summary(),
+            "hbm_peak_gbs": hbm, "peak_source": src, "int8_peak_tops": peak_i8,
+            "clocks": clk.summary(),
             "device_error": pkg._lib.device_error(local)}
     print(json.dumps(line), flush=True)
 
@@ -661,6 +686,7 @@ def run_ours_ep(args, world, rank, local):
     st = {"w1": moe.w1, "w1_qscale": moe.w1_q, "w1_fscale": moe.w1_f,
           "workspace13": torch.empty(R_buf * 2 * cfg.N, dtype=hidden.dtype, device=dev)}
     t_gemm = max_over_ranks(time_w13_gemm(pkg, cfg, st, tr), world)
+    peak_i8 = int8_peak_tops()
     gemm_bytes = w13_algorithmic_bytes(cfg, tr)
     R_loc = int(tr["eft"][-1])
     hbm, _, src = measured_peaks()
@@ -692,7 +718,9 @@ def run_ours_ep(args, world, rank, local):
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": src, "traffic": None, "algorithmic_bytes": gemm_bytes,
                      "launch_ms": t_gemm * 1e3,
-                     "int8_tops": 2 * R_loc * 2 * cfg.N * cfg.K / t_gemm / 1e12},
+                     "int8_tops": 2 * R_loc * 2 * cfg.N * cfg.K / t_gemm / 1e12,
+                     "int8_peak_tops": peak_i8,
+                     "int8_frac": 2 * R_loc * 2 * cfg.N * cfg.K / t_gemm / 1e12 / peak_i8},
     }
     if e2e:
         line["e2e"] = e2e
@@ -780,11 +808,17 @@ def run_ours(args, world, rank, local):
     gemm_ops = 2 * R * 2 * cfg.N * cfg.K
     hbm, bf16, src = measured_peaks()
     achieved = gemm_bytes / t_gemm / 1e9
-    traffic = None
+    traffic, traffic_src = None, None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         key = "w13_gemm_silu_quant" if tr["mm1"] is None else "w13_gemm"
-        traffic = json.loads(tfile.read_text()).get(f"{cfg.name}/{key}")
+        tj = json.loads(tfile.read_text())
+        traffic = tj.get(f"{cfg.name}/{key}")
+        if traffic is not None:
+            traffic_src = ("not measured in this run: dram__bytes_read.sum + "
+                           "dram__bytes_write.sum of one ncu capture, profiles/traffic.json, "
+                           + tj.get("captured", "date not recorded"))
+    peak_i8 = int8_peak_tops()
 
     gpu_launches = 9 * args.steps  # route x3, quant, scales_to_qf x2, w13, w2, unpermute
     line = {
@@ -805,8 +839,12 @@ def run_ours(args, world, rank, local):
                      + (", SiLU*up + requant epilogue)" if tr["mm1"] is None else ")"),
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": src, "traffic": traffic,
+                     "traffic_source": traffic_src,
                      "algorithmic_bytes": gemm_bytes, "launch_ms": t_gemm * 1e3,
-                     "int8_tops": gemm_ops / t_gemm / 1e12},
+                     "int8_tops": gemm_ops / t_gemm / 1e12,
+                     "int8_peak_tops": peak_i8,
+                     "int8_frac": gemm_ops / t_gemm / 1e12 / peak_i8,
+                     "int8_peak_source": "measured in this run (i8moe_int8_mma_peak)"},
     }
     if e2e:
         line["e2e"] = e2e

@@ -468,7 +468,8 @@ def test_forward_against_reference_golden(m, gname, cname, fp, fs, ep, fuse_w13,
 @pytest.mark.parametrize("fuse_w13", [False, True], ids=["w13-store", "w13-silu-epilogue"])
 @pytest.mark.parametrize("cname,tile_m", [("decode", 64), ("mid", 128),
                                            ("large_finite@1024", 64),
-                                           ("large_finite@2048", 128)])
+                                           ("large_finite@2048", 128),
+                                           ("default", 128)])
 def test_forward_config_against_oracle(m, cname, tile_m, fuse_w13, cta_pairs):
     """A whole configuration against the oracle, stage by stage: routing maps,
     int8 activations and their Q/F bit-exact, a2q within one step on rare
@@ -476,7 +477,9 @@ def test_forward_config_against_oracle(m, cname, tile_m, fuse_w13, cta_pairs):
     over 256 experts, top-8 -- a few rows per expert, most in one ragged
     tile, the tile_m 64 variant; mid: 512 tokens over 16 experts, tile_m 128;
     large_finite: the large shape (K=4096, N=1536, E=128, fp16) at 1024 and
-    2048 tokens, with weight F scales that keep every stage finite."""
+    2048 tokens, with weight F scales that keep every stage finite; default:
+    the headline configuration at full size (8192 tokens, 256 experts), the
+    whole forward against one oracle forward."""
     cfg, inp = inputs(cname)
     tr = {}
     out = run_forward(m, cfg, inp, True, True, trace=tr, fuse_w13=fuse_w13)
