@@ -75,6 +75,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: expert-parallel exchange over NVLink peer memory or NCCL")
+    ap.add_argument("--ep-combine", choices=["topk", "rows"], default="topk",
+                    help="N>1, peer exchange: the combine performs the whole top-k unpermute "
+                         "from the peers' mm2 rows (topk), or adds per-rank partial rows (rows)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N eager forwards only (for ncu launch lists); no JSON")
     ap.add_argument("--breakdown", action="store_true",
@@ -611,7 +614,7 @@ def run_ours_ep(args, world, rank, local):
     ops_per_step = 2 * T * k * (2 * cfg.N) * cfg.K + 2 * T * k * cfg.K * cfg.N
     p2p = args.ep_exchange == "p2p"
     if p2p:
-        moe.enable_peer_exchange(T, cfg.K, k, hidden.dtype)
+        moe.enable_peer_exchange(T, cfg.K, k, hidden.dtype, combine=args.ep_combine)
 
     if args.profile_steps:
         for _ in range(args.profile_steps):
@@ -694,8 +697,9 @@ def run_ours_ep(args, world, rank, local):
     del graphs
     if p2p:
         moe.p2p.close()
-    exch = ("NVLink peer-memory dispatch and combine (CUDA IPC, no NCCL call per step)" if p2p
-            else "NCCL all-to-all dispatch and combine")
+    exch = (f"NVLink peer-memory dispatch and combine (CUDA IPC, no NCCL call per step; "
+            f"{'top-k combine: the unpermute reads the peers mm2 rows' if args.ep_combine == 'topk' else 'partial-row combine'})"
+            if p2p else "NCCL all-to-all dispatch and combine")
     line = {
         "metric": metric_name(cfg), "value": world * ops_per_step * args.steps / dt / 1e12, "unit": "TOPS",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -712,8 +716,9 @@ def run_ours_ep(args, world, rank, local):
                              + ", CUDA events, max over ranks"},
         "clocks": clocks,
         # p2p: ep_plan, begin, dispatch, wait, ready, combine; nccl: ep_plan, ep_pack,
-        # ep_combine; plus the 9 of the local forward
-        "gpu_launches": (15 if p2p else 12) * args.steps,
+        # ep_combine; plus the 9 of the local forward (8 with the top-k combine,
+        # which takes over its unpermute)
+        "gpu_launches": ((14 if args.ep_combine == "topk" else 15) if p2p else 12) * args.steps,
         "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel (w13, local experts)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": src, "traffic": None, "algorithmic_bytes": gemm_bytes,

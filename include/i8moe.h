@@ -355,11 +355,32 @@ int i8moe_ep_combine(const void* back, int dtype, const int32_t* pos, int64_t n_
  *                          output buffers in rank order (fp32) into out.
  * `par` is the step number modulo 2 (the same on every rank).  Waits give
  * up after 2 s and set a bit in i8moe_device_error.  No multicast objects
- * are created. */
+ * are created.
+ *
+ * Two combines, chosen when the region is sized:
+ *   I8MOE_EP_COMBINE_ROWS  the local forward ends with the top-k weighted
+ *                          unpermute over this rank's experts (the
+ *                          reference's expert_map skip,
+ *                          moe_permute_unpermute_kernel.inl:133-190) into
+ *                          the region's [capacity, n_hidden] output buffer;
+ *                          i8moe_ep_p2p_combine adds the partial rows.
+ *   I8MOE_EP_COMBINE_TOPK  the local forward stops after the w2 GEMM: its
+ *                          mm2 rows [capacity * topk, n_hidden] and the
+ *                          routing's inverse map [capacity, topk] go into
+ *                          the region's mm2 / inv buffers, and
+ *                          i8moe_ep_p2p_combine_topk performs the top-k
+ *                          weighted unpermute itself, reading every slot's
+ *                          mm2 row from the rank that owns its expert:
+ *                          out[t] = dtype(sum over j in top-k order of
+ *                          w[t, j] * mm2), one fp32 fma chain and one
+ *                          rounding, as the single-GPU unpermute. */
 #define I8MOE_IPC_HANDLE_BYTES 64
+#define I8MOE_EP_COMBINE_ROWS 0
+#define I8MOE_EP_COMBINE_TOPK 1
 
 typedef struct {
   int64_t off_rows, off_ids, off_w, off_out, out_bytes, off_inbox, off_flags, off_epoch;
+  int64_t off_mm2, mm2_bytes, off_inv, inv_bytes; /* per parity; 0 unless COMBINE_TOPK */
   int64_t bytes; /* region size */
 } i8moe_ep_p2p_layout;
 
@@ -373,8 +394,9 @@ typedef struct {
   i8moe_ep_p2p_layout layout;
 } i8moe_ep_p2p;
 
+/* combine: I8MOE_EP_COMBINE_ROWS or I8MOE_EP_COMBINE_TOPK */
 int i8moe_ep_p2p_region_bytes(int64_t n_rank, int64_t capacity, int64_t topk, int64_t n_hidden,
-                              int64_t elem_bytes, i8moe_ep_p2p_layout* layout);
+                              int64_t elem_bytes, int combine, i8moe_ep_p2p_layout* layout);
 /* cudaMalloc'd (zeroed) region and its IPC handle (I8MOE_IPC_HANDLE_BYTES) */
 int i8moe_ep_ipc_alloc(int64_t bytes, void** ptr, uint8_t* handle);
 int i8moe_ep_ipc_open(const uint8_t* handle, void** ptr);
@@ -388,6 +410,13 @@ int i8moe_ep_p2p_wait(const i8moe_ep_p2p* x, int par, i8moe_stream_t stream);
 int i8moe_ep_p2p_ready(const i8moe_ep_p2p* x, int par, i8moe_stream_t stream);
 int i8moe_ep_p2p_combine(const i8moe_ep_p2p* x, int par, int dtype, const int32_t* pos, void* out,
                          i8moe_stream_t stream);
+/* I8MOE_EP_COMBINE_TOPK: waits (bounded) for every destination's output,
+ * then out[t] = dtype(sum_j w[t, j] * mm2_d[inv_d[row_d(t), j]]) in top-k
+ * order with fp32 fmas, d = topk_ids[t, j] / n_local_expert and row_d(t)
+ * the token's receive row at d (its segment offset + pos[t, d]). */
+int i8moe_ep_p2p_combine_topk(const i8moe_ep_p2p* x, int par, int dtype, const int32_t* pos,
+                              const int32_t* topk_ids, const float* topk_weights,
+                              int64_t n_local_expert, void* out, i8moe_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -26,7 +26,7 @@ PROTOTYPES = {
     "i8moe_ep_plan": (I32, [P, I64, I64, I64, I64, P, P, P, P]),
     "i8moe_ep_pack": (I32, [P, I64, P, P, I64, P, I64, I64, P, P, P, P]),
     "i8moe_ep_combine": (I32, [P, I32, P, I64, I64, P, I64, P, P]),
-    "i8moe_ep_p2p_region_bytes": (I32, [I64, I64, I64, I64, I64, P]),
+    "i8moe_ep_p2p_region_bytes": (I32, [I64, I64, I64, I64, I64, I32, P]),
     "i8moe_ep_ipc_alloc": (I32, [I64, P, P]),
     "i8moe_ep_ipc_open": (I32, [P, P]),
     "i8moe_ep_ipc_close": (I32, [P]),
@@ -35,6 +35,7 @@ PROTOTYPES = {
     "i8moe_ep_p2p_wait": (I32, [P, I32, P]),
     "i8moe_ep_p2p_ready": (I32, [P, I32, P]),
     "i8moe_ep_p2p_combine": (I32, [P, I32, I32, P, P, P]),
+    "i8moe_ep_p2p_combine_topk": (I32, [P, I32, I32, P, P, P, I64, P, P]),
     "i8moe_last_error": (c_char_p, []),
     "i8moe_device_error": (I32, [I32, ctypes.POINTER(c_uint32), I32]),
     "i8moe_moe_permute_unpermute_supported": (I32, []),

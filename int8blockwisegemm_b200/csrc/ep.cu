@@ -22,7 +22,11 @@
 //   rows   [C, K]     receive rows         (written by the sources)
 //   ids    [C, k]     their top-k ids       (written by the sources)
 //   w      [C, k]     their top-k weights   (written by the sources)
-//   out    [2][C, K]  local forward output, by step parity (read by sources)
+//   out    [2][C, K]  local forward output, by step parity (read by sources;
+//                     the partial-row combine)
+//   mm2    [2][C*k, K], inv [2][C, k]
+//                     the w2 GEMM output and the routing's inverse map, by
+//                     step parity (read by sources; the top-k combine)
 //   inbox  [2][P][P]  every source's segment lengths, by step parity
 //   flags  [3][P]     epochs: lengths posted, rows posted, output ready
 //   epoch, counter    this rank's step number and a CTA completion counter
@@ -41,7 +45,10 @@
 //   ready:    raise this rank's "output ready" flag at every peer;
 //   combine:  wait for every destination's output, then sum this rank's
 //             tokens' partial rows, read from the peers' memory, in rank
-//             order in fp32.
+//             order in fp32 -- or, with the top-k combine, the local forward
+//             stops after the w2 GEMM and the combine is the whole top-k
+//             weighted unpermute over the peers' mm2 rows, so the output
+//             equals a single-GPU forward bit for bit.
 // Flags carry the step number and waits test flag >= step, so a peer that
 // runs a step ahead never blocks one behind; a peer can never run two
 // steps ahead (a step's dispatch needs every peer's previous output to
@@ -194,6 +201,7 @@ struct P2PArgs {
   int pad_id;                // a global expert id no local expert has
   int par;                   // step parity
   int64_t off_rows, off_ids, off_w, off_out, out_bytes, off_inbox, off_flags, off_epoch;
+  int64_t off_mm2, mm2_bytes, off_inv, inv_bytes;  // top-k combine (per parity)
 };
 
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
@@ -421,6 +429,90 @@ __global__ void __launch_bounds__(256) ep_p2p_combine_kernel(const __grid_consta
   }
 }
 
+// Top-k combine: the unpermute of every token of this rank, over the mm2
+// rows of all ranks.  Slot j of token t was computed by rank
+// d = ids[t, j] / n_local; the token is receive row off_to[d] + pos[t, d]
+// there, and that rank's routing put the slot's mm2 row at
+// inv_d[row * k + j].  out[t] = dtype(fma chain over j in top-k order of
+// w[t, j] * mm2 row, from 0): the arithmetic of the single-GPU unpermute
+// (moe_permute_unpermute_kernel.inl:133-190), so the output equals a
+// single-GPU forward bit for bit.  mm2 rows are read from peer memory, up to
+// eight slots in flight per thread.
+template <typename T>
+__global__ void __launch_bounds__(256) ep_p2p_combine_topk_kernel(
+    const __grid_constant__ P2PArgs a, const int32_t* __restrict__ pos,
+    const int32_t* __restrict__ ids, const float* __restrict__ w, int n_local,
+    T* __restrict__ out) {
+  constexpr int EPC = 8;
+  constexpr int kMaxK = 32;
+  __shared__ int s_off[kMaxRanks];
+  __shared__ const uint4* s_src[kMaxK];  // slot j's mm2 row, or null (skipped)
+  __shared__ float s_w[kMaxK];
+  __shared__ int s_ok;
+  const uint64_t ep = my_epoch(a);
+  if (threadIdx.x == 0) s_ok = wait_flags(a, kFlagOut, ep) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  p2p_offsets(a, s_off);
+  __syncthreads();
+  const int chunks = a.K / EPC;
+  const int64_t max_row = static_cast<int64_t>(a.C) * a.k;
+  for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+    if (threadIdx.x < a.k) {
+      const int j = threadIdx.x;
+      const int e = __ldg(ids + static_cast<int64_t>(t) * a.k + j);
+      const int d = e >= 0 ? e / n_local : -1;
+      const uint4* src = nullptr;
+      if (d >= 0 && d < a.P) {
+        const int p = __ldg(pos + static_cast<int64_t>(t) * a.P + d);
+        const int64_t row = static_cast<int64_t>(s_off[d]) + p;
+        if (p >= 0 && row < a.C) {
+          const int32_t* inv =
+              reinterpret_cast<const int32_t*>(a.base[d] + a.off_inv + a.par * a.inv_bytes);
+          const int prow = __ldcg(inv + row * a.k + j);  // written by rank d
+          if (prow >= 0 && prow < max_row)
+            src = reinterpret_cast<const uint4*>(a.base[d] + a.off_mm2 + a.par * a.mm2_bytes) +
+                  static_cast<int64_t>(prow) * chunks;
+        }
+      }
+      if (src == nullptr) atomicOr(&g_err_ep, kErrBadIndex);  // every slot has an owner
+      s_src[j] = src;
+      s_w[j] = __ldg(w + static_cast<int64_t>(t) * a.k + j);
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+      float acc[EPC];
+#pragma unroll
+      for (int i = 0; i < EPC; ++i) acc[i] = 0.f;
+      constexpr int kU = 8;
+      for (int j0 = 0; j0 < a.k; j0 += kU) {
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int j = j0 + u;
+          if (j < a.k && s_src[j] != nullptr) v[u] = __ldcg(s_src[j] + c);  // peer memory, via L2
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int j = j0 + u;
+          if (j < a.k && s_src[j] != nullptr) {
+            const float wt = s_w[j];
+            const T* x = reinterpret_cast<const T*>(&v[u]);
+#pragma unroll
+            for (int i = 0; i < EPC; ++i) acc[i] = fmaf(wt, Num<T>::to_f(x[i]), acc[i]);
+          }
+        }
+      }
+      uint4 o;
+      T* y = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int i = 0; i < EPC; ++i) y[i] = Num<T>::from_f(acc[i]);
+      reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * a.K)[c] = o;
+    }
+    __syncthreads();  // s_src / s_w are rewritten for the next token
+  }
+}
+
 int offsets_from(const int64_t* counts, int P, RankOffsets* ro) {
   I8_REQUIRE(P >= 1 && P <= kMaxRanks, "ep: the group must have 1..%d ranks", kMaxRanks);
   ro->off[0] = 0;
@@ -475,19 +567,28 @@ int i8moe_ep_pack(const void* hidden, int64_t row_bytes, const int32_t* topk_ids
 }
 
 int i8moe_ep_p2p_region_bytes(int64_t n_rank, int64_t capacity, int64_t topk, int64_t n_hidden,
-                              int64_t elem_bytes, i8moe_ep_p2p_layout* layout) {
+                              int64_t elem_bytes, int combine, i8moe_ep_p2p_layout* layout) {
   I8_REQUIRE(n_rank >= 1 && n_rank <= kMaxRanks, "ep p2p: the group must have 1..%d ranks", kMaxRanks);
   I8_REQUIRE(capacity >= 1 && topk >= 1 && topk <= 32 && n_hidden >= 8 && elem_bytes == 2 &&
                  (n_hidden * elem_bytes) % 16 == 0,
              "ep p2p: bad shape");
+  I8_REQUIRE(combine == I8MOE_EP_COMBINE_ROWS || combine == I8MOE_EP_COMBINE_TOPK,
+             "ep p2p: combine must be I8MOE_EP_COMBINE_ROWS or I8MOE_EP_COMBINE_TOPK");
+  I8_REQUIRE(capacity * topk < (int64_t(1) << 31), "ep p2p: capacity * topk must fit in int32");
   auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  const bool rows = combine == I8MOE_EP_COMBINE_ROWS;
   i8moe_ep_p2p_layout l{};
   int64_t o = 0;
   l.off_rows = o;  o = up(o + capacity * n_hidden * elem_bytes);
   l.off_ids = o;   o = up(o + capacity * topk * 4);
   l.off_w = o;     o = up(o + capacity * topk * 4);
-  l.off_out = o;   l.out_bytes = up(capacity * n_hidden * elem_bytes);
+  // partial rows (ROWS) or mm2 rows + inverse map (TOPK), one per parity
+  l.off_out = o;   l.out_bytes = rows ? up(capacity * n_hidden * elem_bytes) : 0;
   o = up(o + 2 * l.out_bytes);
+  l.off_mm2 = o;   l.mm2_bytes = rows ? 0 : up(capacity * topk * n_hidden * elem_bytes);
+  o = up(o + 2 * l.mm2_bytes);
+  l.off_inv = o;   l.inv_bytes = rows ? 0 : up(capacity * topk * 4);
+  o = up(o + 2 * l.inv_bytes);
   l.off_inbox = o; o = up(o + 2 * n_rank * n_rank * 4);
   l.off_flags = o; o = up(o + 3 * n_rank * 8);
   l.off_epoch = o; o = up(o + 16);  // epoch (8 B), CTA completion counter (4 B)
@@ -565,6 +666,10 @@ int p2p_args(const i8moe_ep_p2p* x, int par, P2PArgs* a) {
   a->off_inbox = x->layout.off_inbox;
   a->off_flags = x->layout.off_flags;
   a->off_epoch = x->layout.off_epoch;
+  a->off_mm2 = x->layout.off_mm2;
+  a->mm2_bytes = x->layout.mm2_bytes;
+  a->off_inv = x->layout.off_inv;
+  a->inv_bytes = x->layout.inv_bytes;
   return I8MOE_OK;
 }
 }  // namespace
@@ -615,6 +720,8 @@ int i8moe_ep_p2p_combine(const i8moe_ep_p2p* x, int par, int dtype, const int32_
   I8_REQUIRE(dtype == I8MOE_BF16 || dtype == I8MOE_FP16, "ep p2p combine: bfloat16 or float16 rows");
   I8_REQUIRE(a.K % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0,
              "ep p2p combine: 16-byte rows");
+  I8_REQUIRE(x->layout.out_bytes >= static_cast<int64_t>(a.C) * a.K * a.esize,
+             "ep p2p combine: the region was not sized with I8MOE_EP_COMBINE_ROWS");
   if (a.T == 0) return I8MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(a.T, 4 * num_sms(current_device())));
@@ -623,6 +730,33 @@ int i8moe_ep_p2p_combine(const i8moe_ep_p2p* x, int par, int dtype, const int32_
   else
     ep_p2p_combine_kernel<__half><<<grid, 256, 0, st>>>(a, pos, static_cast<__half*>(out));
   return check_launch("ep_p2p_combine");
+}
+
+int i8moe_ep_p2p_combine_topk(const i8moe_ep_p2p* x, int par, int dtype, const int32_t* pos,
+                              const int32_t* topk_ids, const float* topk_weights,
+                              int64_t n_local_expert, void* out, i8moe_stream_t stream) {
+  P2PArgs a;
+  int rc = p2p_args(x, par, &a);
+  if (rc) return rc;
+  I8_REQUIRE(dtype == I8MOE_BF16 || dtype == I8MOE_FP16, "ep p2p combine: bfloat16 or float16 rows");
+  I8_REQUIRE(a.K % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0,
+             "ep p2p combine: 16-byte rows");
+  I8_REQUIRE(x->layout.mm2_bytes >= static_cast<int64_t>(a.C) * a.k * a.K * a.esize &&
+                 x->layout.inv_bytes >= static_cast<int64_t>(a.C) * a.k * 4,
+             "ep p2p combine_topk: the region was not sized with I8MOE_EP_COMBINE_TOPK");
+  I8_REQUIRE(n_local_expert >= 1 && n_local_expert < (int64_t(1) << 31),
+             "ep p2p combine_topk: bad n_local_expert");
+  if (a.T == 0) return I8MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(a.T, 4 * num_sms(current_device())));
+  const int nl = static_cast<int>(n_local_expert);
+  if (dtype == I8MOE_BF16)
+    ep_p2p_combine_topk_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        a, pos, topk_ids, topk_weights, nl, static_cast<__nv_bfloat16*>(out));
+  else
+    ep_p2p_combine_topk_kernel<__half><<<grid, 256, 0, st>>>(a, pos, topk_ids, topk_weights, nl,
+                                                             static_cast<__half*>(out));
+  return check_launch("ep_p2p_combine_topk");
 }
 
 int i8moe_ep_combine(const void* back, int dtype, const int32_t* pos, int64_t n_token,

@@ -84,6 +84,8 @@ def _run_cutlass_int8_hybrid_grouped_moe(
     *,
     _trace: dict | None = None,
     _tile_m: int | None = None,
+    _inv_out: torch.Tensor | None = None,
+    _unpermute: bool = True,
 ) -> None:
     """Full INT8 hybrid grouped MoE forward; writes ``output`` [M, K].
 
@@ -92,7 +94,13 @@ def _run_cutlass_int8_hybrid_grouped_moe(
     it for verification.
     ``_tile_m``: forces the quant tile height (64 or 128) instead of the
     rows-per-expert rule; expert parallelism passes the single-GPU choice so
-    its quant tiles match a single-GPU run."""
+    its quant tiles match a single-GPU run.
+    ``_inv_out``: int32 buffer of M * topk elements that receives the
+    routing's inverse map.
+    ``_unpermute=False``: stop after the w2 GEMM; its rows stay in
+    ``workspace2`` ([M * topk, K] at offset 0) and ``output`` is not
+    written.  The expert-parallel top-k combine performs the unpermute from
+    those rows and ``_inv_out`` on the rank that owns each token."""
     assert activation.is_gated, "Only gated activation is supported"
     assert hidden_states.dtype in (torch.float16, torch.bfloat16, torch.float32)
     assert w1.dtype == torch.int8 and w2.dtype == torch.int8
@@ -122,7 +130,8 @@ def _run_cutlass_int8_hybrid_grouped_moe(
     if _USE_FUSED_PERMUTE_QUANT_W1:
         (expert_first_token_offset, inv_perm, permuted_idx, expert_offsets, problem_sizes1,
          problem_sizes2, scale_offsets) = moe_route_for_gemm(
-            topk_ids, M, num_expert, local_E, expert_map, 2 * N, K, K, N, tile_m)
+            topk_ids, M, num_expert, local_E, expert_map, 2 * N, K, K, N, tile_m,
+            inv_out=_inv_out)
         a1q, a1_qscale, a1_fscale, a1_scale_offsets = fused_permute_quant_int8_hybrid_grouped(
             hidden_states, permuted_idx, topk=topk, block_k=quant_block_size, q_max=q_max,
             super_group_size=super_group_size, expert_offsets=expert_offsets, tile_m=tile_m,
@@ -192,5 +201,9 @@ def _run_cutlass_int8_hybrid_grouped_moe(
         if _USE_FUSED_PERMUTE_QUANT_W1:
             _trace["pidx"] = permuted_idx
 
+    if _inv_out is not None and _inv_out.data_ptr() != inv_perm.data_ptr():
+        _inv_out.view(-1).copy_(inv_perm.view(-1))
+    if not _unpermute:
+        return
     moe_unpermute(out=output, permuted_hidden_states=mm2_out, topk_weights=topk_weights,
                   inv_permuted_idx=inv_perm, expert_first_token_offset=expert_first_token_offset)

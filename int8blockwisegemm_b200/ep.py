@@ -16,12 +16,19 @@ all-to-all:
   global rows per expert) the INT8 activation tiles, scales, int32
   accumulators and mm1/mm2 rows of each expert are therefore bit-identical
   to the single-GPU forward.
-* local forward: the top-k weighted unpermute sums this rank's experts of
-  each received token (fp32 in top-k order, then the storage type).
-* combine: the partial rows return to their source ranks, which add them in
-  fp32 in rank order (one segment per rank, so the order is deterministic)
-  and round once.  Only this summation order differs from one GPU, so the
-  output agrees within the reference's tolerance rather than bit for bit.
+* combine, two forms.  Top-k combine (the peer exchange's default): the
+  local forward stops after the w2 GEMM and each source rank performs the
+  whole top-k weighted unpermute of its own tokens, reading every slot's
+  mm2 row from the rank that owns the slot's expert -- fp32 in top-k order
+  and one rounding, so the output equals a single-GPU forward bit for bit
+  and no rank runs an unpermute pass.  Partial-row combine (NCCL, and the
+  peer exchange's "rows" mode): the local forward ends with the unpermute
+  over this rank's experts (the reference's ``expert_map`` skip), the
+  partial rows return to their source ranks, which add them in fp32 in rank
+  order (one segment per rank, so the order is deterministic) and round
+  once; this moves fewer bytes (one row per token and destination rank
+  rather than one per top-k slot) but rounds each partial sum, so the output
+  agrees with one GPU within the reference's tolerance, not bit for bit.
 
 Two exchanges implement that on GPUs.  ``PeerExchange`` (the default of
 ``bench.py``) stores rows straight into the peers' receive buffers over NVLink
@@ -166,7 +173,11 @@ class ExpertParallel:
 
 class _Layout(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int64) for n in ("off_rows", "off_ids", "off_w", "off_out", "out_bytes",
-                                              "off_inbox", "off_flags", "off_epoch", "bytes")]
+                                              "off_inbox", "off_flags", "off_epoch", "off_mm2",
+                                              "mm2_bytes", "off_inv", "inv_bytes", "bytes")]
+
+
+COMBINE_ROWS, COMBINE_TOPK = 0, 1  # I8MOE_EP_COMBINE_ROWS / _TOPK of include/i8moe.h
 
 
 class _P2PDesc(ctypes.Structure):
@@ -195,21 +206,35 @@ class PeerExchange:
     regions through CUDA IPC handles exchanged once over the process group.
     A step runs ep_plan, the dispatch (rows stored straight into the
     destinations' receive buffers), a wait for every source's rows, the
-    local forward over the ``capacity`` receive rows into this step's
-    output buffer, the "output ready" signal and the combine (partial rows
-    read from the peers' output buffers, summed in rank order).  Every shape
-    is static, so whole steps can be captured in CUDA graphs."""
+    local forward over the ``capacity`` receive rows, the "output ready"
+    signal and the combine.  Every shape is static, so whole steps can be
+    captured in CUDA graphs.
+
+    ``combine="topk"`` (the default): the local forward stops after the w2
+    GEMM, writing its mm2 rows and the routing's inverse map into this
+    step's region buffers, and the combine performs the whole top-k
+    weighted unpermute of this rank's tokens from the peers' mm2 rows -- one
+    fp32 fma chain in top-k order and one rounding, so the output equals a
+    single-GPU forward bit for bit, and no rank runs an unpermute pass.
+    ``combine="rows"``: the local forward ends with the unpermute over this
+    rank's experts into the output buffer and the combine adds the returned
+    partial rows in rank order (fewer NVLink bytes: one row per token and
+    destination rank instead of one per top-k slot)."""
 
     def __init__(self, ep: ExpertParallel, max_tokens: int, n_hidden: int, topk: int,
-                 dtype: torch.dtype, device):
+                 dtype: torch.dtype, device, combine: str = "topk"):
         from ._lib import call
         assert dtype in (torch.bfloat16, torch.float16) and ep.world >= 2
+        if combine not in ("topk", "rows"):
+            raise ValueError(f"combine must be 'topk' or 'rows', not {combine!r}")
         self.ep, self.device, self.dtype = ep, torch.device(device), dtype
         P, r = ep.world, ep.rank
         self.P, self.k, self.K, self.T = P, topk, n_hidden, max_tokens
         self.C = P * max_tokens
+        self.combine = combine
         lay = _Layout()
-        call("i8moe_ep_p2p_region_bytes", P, self.C, topk, n_hidden, 2, ctypes.addressof(lay))
+        call("i8moe_ep_p2p_region_bytes", P, self.C, topk, n_hidden, 2,
+             COMBINE_TOPK if combine == "topk" else COMBINE_ROWS, ctypes.addressof(lay))
         ptr, handle = ctypes.c_void_p(), (ctypes.c_uint8 * 64)()
         with torch.cuda.device(self.device):
             call("i8moe_ep_ipc_alloc", lay.bytes, ctypes.addressof(ptr), ctypes.addressof(handle))
@@ -242,8 +267,14 @@ class PeerExchange:
         self.recv_rows = as_t(lay.off_rows, (C, K), "<i2").view(dtype)
         self.recv_ids = as_t(lay.off_ids, (C, k), "<i4")
         self.recv_w = as_t(lay.off_w, (C, k), "<f4")
-        self.out_buf = [as_t(lay.off_out + i * lay.out_bytes, (C, K), "<i2").view(dtype)
-                        for i in range(2)]
+        if combine == "rows":
+            self.out_buf = [as_t(lay.off_out + i * lay.out_bytes, (C, K), "<i2").view(dtype)
+                            for i in range(2)]
+        else:
+            self.mm2_buf = [as_t(lay.off_mm2 + i * lay.mm2_bytes, (C * k, K), "<i2").view(dtype)
+                            for i in range(2)]
+            self.inv_buf = [as_t(lay.off_inv + i * lay.inv_bytes, (C * k,), "<i4")
+                            for i in range(2)]
         self.pos = torch.empty(max_tokens, P, dtype=torch.int32, device=self.device)
         self.lst = torch.empty(P, max_tokens, dtype=torch.int32, device=self.device)
         self.counts = torch.empty(P, dtype=torch.int32, device=self.device)
@@ -251,8 +282,12 @@ class PeerExchange:
         dist.barrier(group=ep.group)  # every region is mapped before any rank writes into one
 
     def forward(self, hidden, topk_ids, topk_weights, local_forward, out=None):
-        """One expert-parallel step; ``local_forward(rows, ids, weights, out)``
-        runs the local experts over the ``capacity`` receive rows into out."""
+        """One expert-parallel step.  ``local_forward(rows, ids, weights, out)``
+        runs the local experts over the ``capacity`` receive rows into out
+        (combine="rows"); with combine="topk" it is called as
+        ``local_forward(rows, ids, weights, None, mm2=..., inv=...)`` and
+        must leave the w2 GEMM rows in ``mm2`` and the inverse map in
+        ``inv`` instead."""
         from ._lib import BF16, FP16, call
         T, k = topk_ids.shape
         assert T <= self.T and k == self.k and hidden.shape[1] == self.K
@@ -272,11 +307,19 @@ class PeerExchange:
             call("i8moe_ep_p2p_dispatch", d, par, hidden.data_ptr(), ids.data_ptr(),
                  wts.data_ptr(), self.lst.data_ptr(), self.counts.data_ptr(), st)
             call("i8moe_ep_p2p_wait", d, par, st)
-        local_forward(self.recv_rows, self.recv_ids, self.recv_w, self.out_buf[par])
         dt = {torch.bfloat16: BF16, torch.float16: FP16}[self.dtype]
+        if self.combine == "rows":
+            local_forward(self.recv_rows, self.recv_ids, self.recv_w, self.out_buf[par])
+            with torch.cuda.device(self.device):
+                call("i8moe_ep_p2p_ready", d, par, st)
+                call("i8moe_ep_p2p_combine", d, par, dt, self.pos.data_ptr(), out.data_ptr(), st)
+            return out
+        local_forward(self.recv_rows, self.recv_ids, self.recv_w, None,
+                      mm2=self.mm2_buf[par], inv=self.inv_buf[par])
         with torch.cuda.device(self.device):
             call("i8moe_ep_p2p_ready", d, par, st)
-            call("i8moe_ep_p2p_combine", d, par, dt, self.pos.data_ptr(), out.data_ptr(), st)
+            call("i8moe_ep_p2p_combine_topk", d, par, dt, self.pos.data_ptr(), ids.data_ptr(),
+                 wts.data_ptr(), self.ep.n_local, out.data_ptr(), st)
         return out
 
     def close(self):
@@ -319,40 +362,60 @@ class EPMoE:
         self.emap = ep.expert_map(w1.device)
         self._ws = None
 
-    def _workspaces(self, rows: int, K: int, N: int, dtype, device):
-        need13, need2 = rows * max(2 * N, K), rows * max(N, K)
-        if self._ws is None or self._ws[0].numel() < need13 or self._ws[0].dtype != dtype:
+    def _workspaces(self, rows: int, K: int, N: int, dtype, device, with_ws2: bool = True):
+        need13, need2 = rows * max(2 * N, K), rows * max(N, K) if with_ws2 else 0
+        if (self._ws is None or self._ws[0].numel() < need13 or self._ws[1].numel() < need2
+                or self._ws[0].dtype != dtype):
             self._ws = (torch.empty(need13, dtype=dtype, device=device),
                         torch.empty(need2, dtype=dtype, device=device))
-        return self._ws[0][:need13].view(rows, -1), self._ws[1][:need2].view(rows, -1)
+        ws2 = self._ws[1][:need2].view(rows, -1) if with_ws2 else None
+        return self._ws[0][:need13].view(rows, -1), ws2
 
-    def local_forward(self, hidden, topk_ids, topk_weights, trace: dict | None = None, out=None):
+    def local_forward(self, hidden, topk_ids, topk_weights, trace: dict | None = None, out=None,
+                      mm2=None, inv=None):
+        """The runner over the received rows with this rank's experts.  With
+        ``mm2`` / ``inv`` (the top-k combine) the w2 GEMM rows go to ``mm2``
+        ([rows * topk, K]), the inverse map to ``inv`` and no unpermute
+        runs."""
         from .activation import MoEActivation
         from .cutlass_runner import _run_cutlass_int8_hybrid_grouped_moe
         T, k = topk_ids.shape
         K, N = hidden.shape[1], self.w2.shape[2]
-        if out is None:
+        topk_combine = mm2 is not None
+        if out is None and not topk_combine:
             out = torch.empty(T, K, dtype=hidden.dtype, device=hidden.device)
         if T == 0:
             return out
-        ws13, ws2 = self._workspaces(T * k, K, N, hidden.dtype, hidden.device)
+        ws13, ws2 = self._workspaces(T * k, K, N, hidden.dtype, hidden.device,
+                                     with_ws2=not topk_combine)
+        if topk_combine:
+            # mm2 is [rows*k, K]: it holds every view the runner takes of
+            # workspace2 ([rows*k, N] and [rows*k, K])
+            assert mm2.shape == (T * k, K) and mm2.dtype == hidden.dtype and N <= K
+            assert inv is not None and inv.numel() == T * k
+            ws2 = mm2
         _run_cutlass_int8_hybrid_grouped_moe(
             out, hidden, self.w1, self.w2, topk_ids, topk_weights, MoEActivation.SILU,
             self.ep.num_experts, self.emap, self.w1_q, self.w1_f, self.w2_q, self.w2_f,
-            ws13, ws2, self.qbs, self.sg, self.q_max, _trace=trace, _tile_m=self.tile_m)
+            ws13, ws2, self.qbs, self.sg, self.q_max, _trace=trace, _tile_m=self.tile_m,
+            _inv_out=inv, _unpermute=not topk_combine)
         return out
 
-    def enable_peer_exchange(self, max_tokens: int, n_hidden: int, topk: int, dtype):
+    def enable_peer_exchange(self, max_tokens: int, n_hidden: int, topk: int, dtype,
+                             combine: str = "topk"):
         """Use the NVLink peer-memory exchange (no NCCL, no host
         synchronisation) for steps of up to ``max_tokens`` tokens per rank."""
-        self.p2p = PeerExchange(self.ep, max_tokens, n_hidden, topk, dtype, self.w1.device)
+        self.p2p = PeerExchange(self.ep, max_tokens, n_hidden, topk, dtype, self.w1.device,
+                                combine=combine)
         return self.p2p
 
     def forward(self, hidden, topk_ids, topk_weights, out=None, trace: dict | None = None):
         p2p = getattr(self, "p2p", None)
         if p2p is not None and hidden.is_cuda:
-            return p2p.forward(hidden, topk_ids, topk_weights,
-                               lambda h, i, w, o: self.local_forward(h, i, w, trace, out=o), out)
+            return p2p.forward(
+                hidden, topk_ids, topk_weights,
+                lambda h, i, w, o, mm2=None, inv=None: self.local_forward(
+                    h, i, w, trace, out=o, mm2=mm2, inv=inv), out)
         return self.ep.forward(
             hidden, topk_ids, topk_weights,
             lambda h, i, w: self.local_forward(h, i, w, trace), out)

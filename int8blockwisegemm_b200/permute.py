@@ -51,9 +51,11 @@ def moe_permute_metadata(hidden_states, topk_ids, n_expert: int, n_local_expert:
 
 
 def moe_route_for_gemm(topk_ids, n_token: int, n_expert: int, n_local_expert: int, expert_map,
-                       n_out1: int, k1: int, n_out2: int, k2: int, tile_m: int):
+                       n_out1: int, k1: int, n_out2: int, k2: int, tile_m: int, inv_out=None):
     """Extension: routing metadata plus the int32 expert offsets, both GEMMs'
     problem sizes and the quant scale offsets, from one set of kernels.
+    ``inv_out`` (int32, n_token * topk elements, contiguous) receives the
+    inverse map instead of a new tensor.
 
     Returns (expert_first_token_offset, inv_permuted_idx (flat), permuted_idx,
              expert_offsets_i32 [E+1], problem_sizes13, problem_sizes2,
@@ -66,7 +68,12 @@ def moe_route_for_gemm(topk_ids, n_token: int, n_expert: int, n_local_expert: in
     rows = n_token * topk
     eft = torch.empty(n_local_expert + 1, dtype=torch.int64, device=dev)
     pidx = torch.empty(rows, dtype=torch.int32, device=dev)
-    inv = torch.empty((n_token, topk), dtype=torch.int32, device=dev)
+    if inv_out is None:
+        inv = torch.empty((n_token, topk), dtype=torch.int32, device=dev)
+    else:
+        assert (inv_out.dtype == torch.int32 and inv_out.is_contiguous()
+                and inv_out.numel() == rows and inv_out.device == dev)
+        inv = inv_out.view(n_token, topk)
     eo = torch.empty(n_local_expert + 1, dtype=torch.int32, device=dev)
     ps1 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)
     ps2 = torch.empty((n_local_expert, 3), dtype=torch.int32, device=dev)

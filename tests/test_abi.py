@@ -87,19 +87,28 @@ def test_peer_exchange_region_layout():
     from int8blockwisegemm_b200.ep import _Layout
     lib = _lib.LIB
     P, T, k, K = 8, 8192, 8, 2048
-    lay = _Layout()
-    assert lib.i8moe_ep_p2p_region_bytes(P, P * T, k, K, 2, ctypes.addressof(lay)) == 0
     C = P * T
-    parts = [(lay.off_rows, C * K * 2), (lay.off_ids, C * k * 4), (lay.off_w, C * k * 4),
-             (lay.off_out, 2 * lay.out_bytes), (lay.off_inbox, 2 * P * P * 4),
-             (lay.off_flags, 3 * P * 8), (lay.off_epoch, 12)]
-    assert lay.out_bytes >= C * K * 2
-    end = 0
-    for off, size in parts:
-        assert off % 256 == 0 and off >= end, (off, end)
-        end = off + size
-    assert end <= lay.bytes
-    assert lib.i8moe_ep_p2p_region_bytes(33, 33, k, K, 2, ctypes.addressof(lay)) == -1
+    for combine in (0, 1):  # I8MOE_EP_COMBINE_ROWS, I8MOE_EP_COMBINE_TOPK
+        lay = _Layout()
+        assert lib.i8moe_ep_p2p_region_bytes(P, C, k, K, 2, combine, ctypes.addressof(lay)) == 0
+        parts = [(lay.off_rows, C * K * 2), (lay.off_ids, C * k * 4), (lay.off_w, C * k * 4),
+                 (lay.off_out, 2 * lay.out_bytes), (lay.off_mm2, 2 * lay.mm2_bytes),
+                 (lay.off_inv, 2 * lay.inv_bytes), (lay.off_inbox, 2 * P * P * 4),
+                 (lay.off_flags, 3 * P * 8), (lay.off_epoch, 12)]
+        if combine == 0:
+            assert lay.out_bytes >= C * K * 2 and lay.mm2_bytes == 0 and lay.inv_bytes == 0
+        else:
+            assert lay.out_bytes == 0 and lay.mm2_bytes >= C * k * K * 2
+            assert lay.inv_bytes >= C * k * 4
+        end = 0
+        for off, size in parts:
+            assert off % 256 == 0 and off >= end, (off, end)
+            end = off + size
+        assert end <= lay.bytes
+    lay = _Layout()
+    assert lib.i8moe_ep_p2p_region_bytes(33, 33, k, K, 2, 0, ctypes.addressof(lay)) == -1
     assert "ranks" in _lib.last_error()
-    assert lib.i8moe_ep_p2p_region_bytes(P, C, k, K, 4, ctypes.addressof(lay)) == -1
-    assert lib.i8moe_ep_p2p_region_bytes(P, C, 33, K, 2, ctypes.addressof(lay)) == -1
+    assert lib.i8moe_ep_p2p_region_bytes(P, C, k, K, 4, 0, ctypes.addressof(lay)) == -1
+    assert lib.i8moe_ep_p2p_region_bytes(P, C, 33, K, 2, 0, ctypes.addressof(lay)) == -1
+    assert lib.i8moe_ep_p2p_region_bytes(P, C, k, K, 2, 2, ctypes.addressof(lay)) == -1
+    assert "combine" in _lib.last_error()

@@ -2,10 +2,14 @@
 Each rank runs the EP forward (dispatch -> sm_100a forward of its local
 experts -> combine) and, on its own GPU, the single-GPU forward of all
 tokens; per local expert the INT8 activations, mm1, a2q and mm2 rows must be
-bit-identical, and the combined output within the reference tolerance
-(max-abs-rel 1e-2).  The peer-memory exchange also runs steps of both
-parities and two steps captured in a CUDA graph and replayed.  Needs two
-GPUs; skipped otherwise."""
+bit-identical.  The combined output must equal the single-GPU output bit for
+bit with the peer exchange's top-k combine (the unpermute runs whole on the
+token's own rank), and agree within the reference tolerance (max-abs-rel
+1e-2) with the partial-row combines (NCCL, and the peer exchange's "rows"
+mode), which add per-rank partial sums.  The peer-memory exchange also runs
+steps of both parities and two steps captured in a CUDA graph and replayed.
+The two-rank tests need two GPUs and are skipped otherwise; the one-GPU
+tests below drive the peer kernels over two local regions."""
 
 import os
 import socket
@@ -67,14 +71,19 @@ def _worker(rank, world, port, cfg_name, mode, errq):
         h_in = d["hidden"][sl].contiguous()
         i_in = d["topk_ids"][sl].contiguous()
         w_in = d["topk_weights"][sl].contiguous()
-        if mode == "p2p":
-            moe.enable_peer_exchange(per, cfg.K, k, dt)
+        p2p = mode.startswith("p2p")
+        if p2p:
+            moe.enable_peer_exchange(per, cfg.K, k, dt,
+                                     combine="rows" if mode == "p2p_rows" else "topk")
         tr = {}
         out = moe.forward(h_in, i_in, w_in, trace=tr)
         torch.cuda.synchronize()
         ref = full_out[sl].float()
 
         def check(o, what):
+            if mode == "p2p":  # top-k combine: the single-GPU arithmetic
+                assert torch.equal(o, full_out[sl]), f"rank {rank} {what}: EP output differs"
+                return
             rel = ((o.float() - ref).abs().max() / ref.abs().max()).item()
             assert rel <= 1e-2, f"rank {rank} {what}: EP output max-abs-rel {rel:.3e} > 1e-2"
 
@@ -91,7 +100,7 @@ def _worker(rank, world, port, cfg_name, mode, errq):
                     assert full_tr[name] is None
                     continue
                 assert torch.equal(tr[name][a:b], full_tr[name][fa:fb]), f"{name} of expert {e}"
-        if mode == "p2p":
+        if p2p:
             # the other step parity, eagerly; then two steps in a CUDA graph
             first = out.clone()
             out2 = moe.forward(h_in, i_in, w_in)
@@ -118,7 +127,7 @@ def _worker(rank, world, port, cfg_name, mode, errq):
         raise
 
 
-@pytest.mark.parametrize("mode", ["nccl", "p2p"])
+@pytest.mark.parametrize("mode", ["nccl", "p2p", "p2p_rows"])
 @pytest.mark.parametrize("cfg_name", ["mid", "default"])
 def test_ep_two_gpus_matches_single_gpu(cfg_name, mode):
     if torch.cuda.device_count() < WORLD:
@@ -161,7 +170,7 @@ def test_p2p_dispatch_peer_timeout_one_gpu():
     torch.cuda.set_device(dev)
     P, T, k, K = 2, 64, 4, 256
     lay = _Layout()
-    call("i8moe_ep_p2p_region_bytes", P, P * T, k, K, 2, ctypes.addressof(lay))
+    call("i8moe_ep_p2p_region_bytes", P, P * T, k, K, 2, 0, ctypes.addressof(lay))
     regions = [torch.zeros(lay.bytes, dtype=torch.uint8, device=dev) for _ in range(P)]
     desc = _P2PDesc()
     for d in range(P):
@@ -192,3 +201,82 @@ def test_p2p_dispatch_peer_timeout_one_gpu():
         epoch = regions[0][lay.off_epoch:lay.off_epoch + 8].view(torch.int64).item()
         assert epoch == step + 1
     assert pkg._lib.device_error(0) == 0
+
+
+def test_p2p_combine_topk_one_gpu():
+    """The top-k combine kernel over two local regions, as rank 1 of 2.
+    Both destinations' mm2 rows and inverse maps are filled on the host, the
+    segment lengths rank 0 sent to each destination go into rank 1's inbox
+    (so rank 1's segments start past them), and every "output ready" flag is
+    raised before the launch, so no wait spins.  The output must equal the
+    single-GPU unpermute of the same rows (the same fma chain in top-k
+    order), for both step parities."""
+    import ctypes
+
+    import int8blockwisegemm_b200 as pkg
+    from int8blockwisegemm_b200._lib import BF16, call
+    from int8blockwisegemm_b200.ep import COMBINE_TOPK, _Layout, _P2PDesc
+    from int8blockwisegemm_b200.permute import moe_unpermute
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    P, T, k, K, E = 2, 64, 4, 256, 16
+    n_local, C = E // P, P * T
+    lay = _Layout()
+    call("i8moe_ep_p2p_region_bytes", P, C, k, K, 2, COMBINE_TOPK, ctypes.addressof(lay))
+    assert lay.out_bytes == 0 and lay.mm2_bytes >= C * k * K * 2 and lay.inv_bytes >= C * k * 4
+    regions = [torch.zeros(lay.bytes, dtype=torch.uint8, device=dev) for _ in range(P)]
+    desc = _P2PDesc()
+    for d in range(P):
+        desc.bases[d] = regions[d].data_ptr()
+    desc.n_rank, desc.rank, desc.n_token, desc.capacity = P, 1, T, C
+    desc.topk, desc.n_hidden, desc.elem_bytes, desc.pad_expert = k, K, 2, 0
+    desc.layout = lay
+    g = torch.Generator().manual_seed(3)
+    # distinct experts per token, as top-k gives
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    w = torch.rand(T, k, generator=g)
+    owner = ids // n_local
+    pos = torch.full((T, P), -1, dtype=torch.int32)  # slot in each destination's segment
+    for dd in range(P):
+        members = (owner == dd).any(dim=1).nonzero().flatten()
+        pos[members, dd] = torch.arange(members.numel(), dtype=torch.int32)
+    sent_by_rank0 = [5, 9]  # rows rank 0 placed first in each destination's receive buffer
+    st = torch.cuda.current_stream(dev).cuda_stream
+    pkg._lib.device_error(0, clear=True)
+    for step in range(2):
+        par = step & 1
+        mm2 = [torch.randn(C * k, K, generator=g).to(torch.bfloat16) for _ in range(P)]
+        gathered = torch.empty(T * k, K, dtype=torch.bfloat16)
+        for dd in range(P):
+            inv = torch.full((C * k,), -1, dtype=torch.int32)
+            perm = torch.randperm(C * k, generator=g).to(torch.int32)
+            inv[:] = perm  # any row of mm2; every slot reads one
+            r = regions[dd]
+            r[lay.off_mm2 + par * lay.mm2_bytes:][:C * k * K * 2].copy_(
+                mm2[dd].view(torch.uint8).flatten().to(dev))
+            r[lay.off_inv + par * lay.inv_bytes:][:C * k * 4].copy_(
+                inv.view(torch.uint8).to(dev))
+            for t in range(T):
+                for j in range(k):
+                    if owner[t, j] == dd:
+                        row = sent_by_rank0[dd] + int(pos[t, dd])
+                        gathered[t * k + j] = mm2[dd][int(inv[row * k + j])]
+        inbox = torch.zeros(2, P, P, dtype=torch.int32)
+        inbox[par, 0] = torch.tensor(sent_by_rank0, dtype=torch.int32)
+        r1 = regions[1]
+        r1[lay.off_inbox:][:2 * P * P * 4].copy_(inbox.view(torch.uint8).flatten().to(dev))
+        flags = torch.full((3, P), step + 1, dtype=torch.int64)
+        r1[lay.off_flags:][:3 * P * 8].copy_(flags.view(torch.uint8).flatten().to(dev))
+        r1[lay.off_epoch:][:8].copy_(torch.tensor([step + 1], dtype=torch.int64)
+                                     .view(torch.uint8).to(dev))
+        ids_d, w_d, pos_d = ids.to(dev), w.to(dev), pos.to(dev)
+        out = torch.empty(T, K, dtype=torch.bfloat16, device=dev)
+        call("i8moe_ep_p2p_combine_topk", ctypes.addressof(desc), par, BF16, pos_d.data_ptr(),
+             ids_d.data_ptr(), w_d.data_ptr(), n_local, out.data_ptr(), st)
+        ref = torch.empty(T, K, dtype=torch.bfloat16, device=dev)
+        moe_unpermute(ref, gathered.to(dev), w_d, torch.arange(T * k, dtype=torch.int32,
+                                                                 device=dev))
+        torch.cuda.synchronize()
+        assert pkg._lib.device_error(0, clear=True) == 0
+        assert torch.equal(out, ref), f"step {step}: top-k combine differs from the unpermute"
