@@ -75,9 +75,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: expert-parallel exchange over NVLink peer memory or NCCL")
-    ap.add_argument("--ep-combine", choices=["topk", "rows"], default="topk",
-                    help="N>1, peer exchange: the combine performs the whole top-k unpermute "
-                         "from the peers' mm2 rows (topk), or adds per-rank partial rows (rows)")
+    ap.add_argument("--ep-combine", choices=["rows", "topk"], default="rows",
+                    help="N>1, peer exchange: the combine adds per-rank partial rows (rows), or "
+                         "performs the whole top-k unpermute from the peers' mm2 rows (topk: "
+                         "bit-identical to one GPU, more NVLink bytes)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N eager forwards only (for ncu launch lists); no JSON")
     ap.add_argument("--breakdown", action="store_true",

@@ -357,7 +357,8 @@ int i8moe_ep_combine(const void* back, int dtype, const int32_t* pos, int64_t n_
  * up after 2 s and set a bit in i8moe_device_error.  No multicast objects
  * are created.
  *
- * Two combines, chosen when the region is sized:
+ * Two combines, chosen when the region is sized (ROWS moves fewer NVLink
+ * bytes; TOPK gives the single-GPU result bit for bit):
  *   I8MOE_EP_COMBINE_ROWS  the local forward ends with the top-k weighted
  *                          unpermute over this rank's experts (the
  *                          reference's expert_map skip,

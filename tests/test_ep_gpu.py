@@ -75,6 +75,7 @@ def _worker(rank, world, port, cfg_name, mode, errq):
         if p2p:
             moe.enable_peer_exchange(per, cfg.K, k, dt,
                                      combine="rows" if mode == "p2p_rows" else "topk")
+            assert moe.p2p.combine == ("rows" if mode == "p2p_rows" else "topk")
         tr = {}
         out = moe.forward(h_in, i_in, w_in, trace=tr)
         torch.cuda.synchronize()
