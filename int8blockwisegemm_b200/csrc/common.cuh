@@ -411,6 +411,80 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
       : "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit TMEM columns, multiplied by q and added to
+// (tmem_mad16) or written into (tmem_mul16) sixteen int32 sums of this thread:
+// the load, its wait and the sixteen integer multiplies in one asm block, so
+// the loaded values live only in block-local registers.
+__device__ __forceinline__ void tmem_mad16(
+    uint32_t taddr, int q,
+    int32_t& w0, int32_t& w1, int32_t& w2, int32_t& w3,
+    int32_t& w4, int32_t& w5, int32_t& w6, int32_t& w7,
+    int32_t& w8, int32_t& w9, int32_t& w10, int32_t& w11,
+    int32_t& w12, int32_t& w13, int32_t& w14, int32_t& w15) {
+  asm volatile(
+      "{\n\t.reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15;\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n\t"
+      "mad.lo.s32 %0, t0, %17, %0;\n\t"
+      "mad.lo.s32 %1, t1, %17, %1;\n\t"
+      "mad.lo.s32 %2, t2, %17, %2;\n\t"
+      "mad.lo.s32 %3, t3, %17, %3;\n\t"
+      "mad.lo.s32 %4, t4, %17, %4;\n\t"
+      "mad.lo.s32 %5, t5, %17, %5;\n\t"
+      "mad.lo.s32 %6, t6, %17, %6;\n\t"
+      "mad.lo.s32 %7, t7, %17, %7;\n\t"
+      "mad.lo.s32 %8, t8, %17, %8;\n\t"
+      "mad.lo.s32 %9, t9, %17, %9;\n\t"
+      "mad.lo.s32 %10, t10, %17, %10;\n\t"
+      "mad.lo.s32 %11, t11, %17, %11;\n\t"
+      "mad.lo.s32 %12, t12, %17, %12;\n\t"
+      "mad.lo.s32 %13, t13, %17, %13;\n\t"
+      "mad.lo.s32 %14, t14, %17, %14;\n\t"
+      "mad.lo.s32 %15, t15, %17, %15;\n\t"
+      "}"
+      : "+r"(w0), "+r"(w1), "+r"(w2), "+r"(w3),
+        "+r"(w4), "+r"(w5), "+r"(w6), "+r"(w7),
+        "+r"(w8), "+r"(w9), "+r"(w10), "+r"(w11),
+        "+r"(w12), "+r"(w13), "+r"(w14), "+r"(w15)
+      : "r"(taddr), "r"(q)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_mul16(
+    uint32_t taddr, int q,
+    int32_t& w0, int32_t& w1, int32_t& w2, int32_t& w3,
+    int32_t& w4, int32_t& w5, int32_t& w6, int32_t& w7,
+    int32_t& w8, int32_t& w9, int32_t& w10, int32_t& w11,
+    int32_t& w12, int32_t& w13, int32_t& w14, int32_t& w15) {
+  asm volatile(
+      "{\n\t.reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15;\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n\t"
+      "mul.lo.s32 %0, t0, %17;\n\t"
+      "mul.lo.s32 %1, t1, %17;\n\t"
+      "mul.lo.s32 %2, t2, %17;\n\t"
+      "mul.lo.s32 %3, t3, %17;\n\t"
+      "mul.lo.s32 %4, t4, %17;\n\t"
+      "mul.lo.s32 %5, t5, %17;\n\t"
+      "mul.lo.s32 %6, t6, %17;\n\t"
+      "mul.lo.s32 %7, t7, %17;\n\t"
+      "mul.lo.s32 %8, t8, %17;\n\t"
+      "mul.lo.s32 %9, t9, %17;\n\t"
+      "mul.lo.s32 %10, t10, %17;\n\t"
+      "mul.lo.s32 %11, t11, %17;\n\t"
+      "mul.lo.s32 %12, t12, %17;\n\t"
+      "mul.lo.s32 %13, t13, %17;\n\t"
+      "mul.lo.s32 %14, t14, %17;\n\t"
+      "mul.lo.s32 %15, t15, %17;\n\t"
+      "}"
+      : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3),
+        "=r"(w4), "=r"(w5), "=r"(w6), "=r"(w7),
+        "=r"(w8), "=r"(w9), "=r"(w10), "=r"(w11),
+        "=r"(w12), "=r"(w13), "=r"(w14), "=r"(w15)
+      : "r"(taddr), "r"(q)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

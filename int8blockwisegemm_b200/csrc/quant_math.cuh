@@ -194,20 +194,11 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   return r;
 }
 
-// two 16-bit values of one word -> their float32 values as an f32x2 pair
-template <typename T>
-__device__ __forceinline__ uint64_t f2_from16(uint32_t w) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    return (static_cast<uint64_t>(w & 0xFFFF0000u) << 32) | static_cast<uint32_t>(w << 16);
-  } else {
-    const __half2 h = *reinterpret_cast<const __half2*>(&w);
-    const float2 f = __half22float2(h);
-    return f2_pack(f.x, f.y);
-  }
-}
-
 // Fast path for one 8-element chunk of bf16 / fp16: the eight int8 values in
-// out; false if the chunk needs the exact path.
+// out; false if the chunk needs the exact path.  Each 32-bit word (two
+// values) goes through one asm block: unpack to an f32x2 pair, the two
+// bracketing FMAs, the agreement sum and the byte extraction, with the pairs
+// built by mov.b64 inside the block.
 template <typename T>
 __device__ __forceinline__ bool quant_chunk_bracket(const uint4& v, const QuantInv& qi,
                                                     uint2& out) {
@@ -220,13 +211,35 @@ __device__ __forceinline__ bool quant_chunk_bracket(const uint4& v, const QuantI
   uint64_t s = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint64_t x = f2_from16<T>(w[i]);
-    const uint64_t ta = f2_fma(x, lo2, m2);
-    const uint64_t tb = f2_fma(x, hi2, m2);
-    const uint64_t d = f2_sub(ta, tb);
-    s = f2_fma(d, d, s);
-    // low byte of each lane's integer, lanes 0 and 1 in bytes 0 and 1
-    b[i] = __byte_perm(static_cast<uint32_t>(ta), static_cast<uint32_t>(ta >> 32), 0x0040);
+    // b[i]: the low byte of each lane's integer, lanes 0 and 1 in bytes 0, 1
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      asm("{\n\t.reg .b32 x0, x1, a0, a1;\n\t.reg .b64 x, ta, tb, dd;\n\t"
+          "shl.b32 x0, %2, 16;\n\t"
+          "and.b32 x1, %2, 0xFFFF0000;\n\t"
+          "mov.b64 x, {x0, x1};\n\t"
+          "fma.rn.f32x2 ta, x, %3, %5;\n\t"
+          "fma.rn.f32x2 tb, x, %4, %5;\n\t"
+          "sub.rn.f32x2 dd, ta, tb;\n\t"
+          "fma.rn.f32x2 %1, dd, dd, %1;\n\t"
+          "mov.b64 {a0, a1}, ta;\n\t"
+          "prmt.b32 %0, a0, a1, 0x0040;\n\t}"
+          : "=r"(b[i]), "+l"(s)
+          : "r"(w[i]), "l"(lo2), "l"(hi2), "l"(m2));
+    } else {
+      asm("{\n\t.reg .b16 h0, h1;\n\t.reg .b32 x0, x1, a0, a1;\n\t.reg .b64 x, ta, tb, dd;\n\t"
+          "mov.b32 {h0, h1}, %2;\n\t"
+          "cvt.f32.f16 x0, h0;\n\t"
+          "cvt.f32.f16 x1, h1;\n\t"
+          "mov.b64 x, {x0, x1};\n\t"
+          "fma.rn.f32x2 ta, x, %3, %5;\n\t"
+          "fma.rn.f32x2 tb, x, %4, %5;\n\t"
+          "sub.rn.f32x2 dd, ta, tb;\n\t"
+          "fma.rn.f32x2 %1, dd, dd, %1;\n\t"
+          "mov.b64 {a0, a1}, ta;\n\t"
+          "prmt.b32 %0, a0, a1, 0x0040;\n\t}"
+          : "=r"(b[i]), "+l"(s)
+          : "r"(w[i]), "l"(lo2), "l"(hi2), "l"(m2));
+    }
   }
   out.x = __byte_perm(b[0], b[1], 0x5410);
   out.y = __byte_perm(b[2], b[3], 0x5410);
