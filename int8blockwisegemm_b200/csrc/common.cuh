@@ -215,6 +215,9 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+__device__ __forceinline__ void bulk_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
@@ -482,6 +485,216 @@ __device__ __forceinline__ void tmem_mul16(
         "=r"(w8), "=r"(w9), "=r"(w10), "=r"(w11),
         "=r"(w12), "=r"(w13), "=r"(w14), "=r"(w15)
       : "r"(taddr), "r"(q)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive TMEM columns multiplied by q and added to
+// (mad) or written into (mul) 32 int32 sums w[0..31] (indices that resolve
+// to registers after inlining).  The _release forms then hand the
+// accumulator back: tcgen05.fence::before_thread_sync and an arrive of this
+// thread on the mbarrier `bar` (shared::cta), right after the load has
+// landed, before the multiplies.  `bar` is ignored by the other forms.
+__device__ __forceinline__ void tmem_mad32(uint32_t taddr, int q, uint32_t bar, int32_t* w) {
+  asm volatile(
+      "{\n\t.reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31;\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n\t"
+      "mad.lo.s32 %0, t0, %33, %0;\n\t"
+      "mad.lo.s32 %1, t1, %33, %1;\n\t"
+      "mad.lo.s32 %2, t2, %33, %2;\n\t"
+      "mad.lo.s32 %3, t3, %33, %3;\n\t"
+      "mad.lo.s32 %4, t4, %33, %4;\n\t"
+      "mad.lo.s32 %5, t5, %33, %5;\n\t"
+      "mad.lo.s32 %6, t6, %33, %6;\n\t"
+      "mad.lo.s32 %7, t7, %33, %7;\n\t"
+      "mad.lo.s32 %8, t8, %33, %8;\n\t"
+      "mad.lo.s32 %9, t9, %33, %9;\n\t"
+      "mad.lo.s32 %10, t10, %33, %10;\n\t"
+      "mad.lo.s32 %11, t11, %33, %11;\n\t"
+      "mad.lo.s32 %12, t12, %33, %12;\n\t"
+      "mad.lo.s32 %13, t13, %33, %13;\n\t"
+      "mad.lo.s32 %14, t14, %33, %14;\n\t"
+      "mad.lo.s32 %15, t15, %33, %15;\n\t"
+      "mad.lo.s32 %16, t16, %33, %16;\n\t"
+      "mad.lo.s32 %17, t17, %33, %17;\n\t"
+      "mad.lo.s32 %18, t18, %33, %18;\n\t"
+      "mad.lo.s32 %19, t19, %33, %19;\n\t"
+      "mad.lo.s32 %20, t20, %33, %20;\n\t"
+      "mad.lo.s32 %21, t21, %33, %21;\n\t"
+      "mad.lo.s32 %22, t22, %33, %22;\n\t"
+      "mad.lo.s32 %23, t23, %33, %23;\n\t"
+      "mad.lo.s32 %24, t24, %33, %24;\n\t"
+      "mad.lo.s32 %25, t25, %33, %25;\n\t"
+      "mad.lo.s32 %26, t26, %33, %26;\n\t"
+      "mad.lo.s32 %27, t27, %33, %27;\n\t"
+      "mad.lo.s32 %28, t28, %33, %28;\n\t"
+      "mad.lo.s32 %29, t29, %33, %29;\n\t"
+      "mad.lo.s32 %30, t30, %33, %30;\n\t"
+      "mad.lo.s32 %31, t31, %33, %31;\n\t"
+      "}"
+      : "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3]),
+        "+r"(w[4]), "+r"(w[5]), "+r"(w[6]), "+r"(w[7]),
+        "+r"(w[8]), "+r"(w[9]), "+r"(w[10]), "+r"(w[11]),
+        "+r"(w[12]), "+r"(w[13]), "+r"(w[14]), "+r"(w[15]),
+        "+r"(w[16]), "+r"(w[17]), "+r"(w[18]), "+r"(w[19]),
+        "+r"(w[20]), "+r"(w[21]), "+r"(w[22]), "+r"(w[23]),
+        "+r"(w[24]), "+r"(w[25]), "+r"(w[26]), "+r"(w[27]),
+        "+r"(w[28]), "+r"(w[29]), "+r"(w[30]), "+r"(w[31])
+      : "r"(taddr), "r"(q), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_mul32(uint32_t taddr, int q, uint32_t bar, int32_t* w) {
+  asm volatile(
+      "{\n\t.reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31;\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n\t"
+      "mul.lo.s32 %0, t0, %33;\n\t"
+      "mul.lo.s32 %1, t1, %33;\n\t"
+      "mul.lo.s32 %2, t2, %33;\n\t"
+      "mul.lo.s32 %3, t3, %33;\n\t"
+      "mul.lo.s32 %4, t4, %33;\n\t"
+      "mul.lo.s32 %5, t5, %33;\n\t"
+      "mul.lo.s32 %6, t6, %33;\n\t"
+      "mul.lo.s32 %7, t7, %33;\n\t"
+      "mul.lo.s32 %8, t8, %33;\n\t"
+      "mul.lo.s32 %9, t9, %33;\n\t"
+      "mul.lo.s32 %10, t10, %33;\n\t"
+      "mul.lo.s32 %11, t11, %33;\n\t"
+      "mul.lo.s32 %12, t12, %33;\n\t"
+      "mul.lo.s32 %13, t13, %33;\n\t"
+      "mul.lo.s32 %14, t14, %33;\n\t"
+      "mul.lo.s32 %15, t15, %33;\n\t"
+      "mul.lo.s32 %16, t16, %33;\n\t"
+      "mul.lo.s32 %17, t17, %33;\n\t"
+      "mul.lo.s32 %18, t18, %33;\n\t"
+      "mul.lo.s32 %19, t19, %33;\n\t"
+      "mul.lo.s32 %20, t20, %33;\n\t"
+      "mul.lo.s32 %21, t21, %33;\n\t"
+      "mul.lo.s32 %22, t22, %33;\n\t"
+      "mul.lo.s32 %23, t23, %33;\n\t"
+      "mul.lo.s32 %24, t24, %33;\n\t"
+      "mul.lo.s32 %25, t25, %33;\n\t"
+      "mul.lo.s32 %26, t26, %33;\n\t"
+      "mul.lo.s32 %27, t27, %33;\n\t"
+      "mul.lo.s32 %28, t28, %33;\n\t"
+      "mul.lo.s32 %29, t29, %33;\n\t"
+      "mul.lo.s32 %30, t30, %33;\n\t"
+      "mul.lo.s32 %31, t31, %33;\n\t"
+      "}"
+      : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]),
+        "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7]),
+        "=r"(w[8]), "=r"(w[9]), "=r"(w[10]), "=r"(w[11]),
+        "=r"(w[12]), "=r"(w[13]), "=r"(w[14]), "=r"(w[15]),
+        "=r"(w[16]), "=r"(w[17]), "=r"(w[18]), "=r"(w[19]),
+        "=r"(w[20]), "=r"(w[21]), "=r"(w[22]), "=r"(w[23]),
+        "=r"(w[24]), "=r"(w[25]), "=r"(w[26]), "=r"(w[27]),
+        "=r"(w[28]), "=r"(w[29]), "=r"(w[30]), "=r"(w[31])
+      : "r"(taddr), "r"(q), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_mad32_release(uint32_t taddr, int q, uint32_t bar, int32_t* w) {
+  asm volatile(
+      "{\n\t.reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31;\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n\t"
+      "tcgen05.fence::before_thread_sync;\n\t"
+      "mbarrier.arrive.shared::cta.b64 _, [%34];\n\t"
+      "mad.lo.s32 %0, t0, %33, %0;\n\t"
+      "mad.lo.s32 %1, t1, %33, %1;\n\t"
+      "mad.lo.s32 %2, t2, %33, %2;\n\t"
+      "mad.lo.s32 %3, t3, %33, %3;\n\t"
+      "mad.lo.s32 %4, t4, %33, %4;\n\t"
+      "mad.lo.s32 %5, t5, %33, %5;\n\t"
+      "mad.lo.s32 %6, t6, %33, %6;\n\t"
+      "mad.lo.s32 %7, t7, %33, %7;\n\t"
+      "mad.lo.s32 %8, t8, %33, %8;\n\t"
+      "mad.lo.s32 %9, t9, %33, %9;\n\t"
+      "mad.lo.s32 %10, t10, %33, %10;\n\t"
+      "mad.lo.s32 %11, t11, %33, %11;\n\t"
+      "mad.lo.s32 %12, t12, %33, %12;\n\t"
+      "mad.lo.s32 %13, t13, %33, %13;\n\t"
+      "mad.lo.s32 %14, t14, %33, %14;\n\t"
+      "mad.lo.s32 %15, t15, %33, %15;\n\t"
+      "mad.lo.s32 %16, t16, %33, %16;\n\t"
+      "mad.lo.s32 %17, t17, %33, %17;\n\t"
+      "mad.lo.s32 %18, t18, %33, %18;\n\t"
+      "mad.lo.s32 %19, t19, %33, %19;\n\t"
+      "mad.lo.s32 %20, t20, %33, %20;\n\t"
+      "mad.lo.s32 %21, t21, %33, %21;\n\t"
+      "mad.lo.s32 %22, t22, %33, %22;\n\t"
+      "mad.lo.s32 %23, t23, %33, %23;\n\t"
+      "mad.lo.s32 %24, t24, %33, %24;\n\t"
+      "mad.lo.s32 %25, t25, %33, %25;\n\t"
+      "mad.lo.s32 %26, t26, %33, %26;\n\t"
+      "mad.lo.s32 %27, t27, %33, %27;\n\t"
+      "mad.lo.s32 %28, t28, %33, %28;\n\t"
+      "mad.lo.s32 %29, t29, %33, %29;\n\t"
+      "mad.lo.s32 %30, t30, %33, %30;\n\t"
+      "mad.lo.s32 %31, t31, %33, %31;\n\t"
+      "}"
+      : "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3]),
+        "+r"(w[4]), "+r"(w[5]), "+r"(w[6]), "+r"(w[7]),
+        "+r"(w[8]), "+r"(w[9]), "+r"(w[10]), "+r"(w[11]),
+        "+r"(w[12]), "+r"(w[13]), "+r"(w[14]), "+r"(w[15]),
+        "+r"(w[16]), "+r"(w[17]), "+r"(w[18]), "+r"(w[19]),
+        "+r"(w[20]), "+r"(w[21]), "+r"(w[22]), "+r"(w[23]),
+        "+r"(w[24]), "+r"(w[25]), "+r"(w[26]), "+r"(w[27]),
+        "+r"(w[28]), "+r"(w[29]), "+r"(w[30]), "+r"(w[31])
+      : "r"(taddr), "r"(q), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_mul32_release(uint32_t taddr, int q, uint32_t bar, int32_t* w) {
+  asm volatile(
+      "{\n\t.reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31;\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {t0, t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12, t13, t14, t15, t16, t17, t18, t19, t20, t21, t22, t23, t24, t25, t26, t27, t28, t29, t30, t31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n\t"
+      "tcgen05.fence::before_thread_sync;\n\t"
+      "mbarrier.arrive.shared::cta.b64 _, [%34];\n\t"
+      "mul.lo.s32 %0, t0, %33;\n\t"
+      "mul.lo.s32 %1, t1, %33;\n\t"
+      "mul.lo.s32 %2, t2, %33;\n\t"
+      "mul.lo.s32 %3, t3, %33;\n\t"
+      "mul.lo.s32 %4, t4, %33;\n\t"
+      "mul.lo.s32 %5, t5, %33;\n\t"
+      "mul.lo.s32 %6, t6, %33;\n\t"
+      "mul.lo.s32 %7, t7, %33;\n\t"
+      "mul.lo.s32 %8, t8, %33;\n\t"
+      "mul.lo.s32 %9, t9, %33;\n\t"
+      "mul.lo.s32 %10, t10, %33;\n\t"
+      "mul.lo.s32 %11, t11, %33;\n\t"
+      "mul.lo.s32 %12, t12, %33;\n\t"
+      "mul.lo.s32 %13, t13, %33;\n\t"
+      "mul.lo.s32 %14, t14, %33;\n\t"
+      "mul.lo.s32 %15, t15, %33;\n\t"
+      "mul.lo.s32 %16, t16, %33;\n\t"
+      "mul.lo.s32 %17, t17, %33;\n\t"
+      "mul.lo.s32 %18, t18, %33;\n\t"
+      "mul.lo.s32 %19, t19, %33;\n\t"
+      "mul.lo.s32 %20, t20, %33;\n\t"
+      "mul.lo.s32 %21, t21, %33;\n\t"
+      "mul.lo.s32 %22, t22, %33;\n\t"
+      "mul.lo.s32 %23, t23, %33;\n\t"
+      "mul.lo.s32 %24, t24, %33;\n\t"
+      "mul.lo.s32 %25, t25, %33;\n\t"
+      "mul.lo.s32 %26, t26, %33;\n\t"
+      "mul.lo.s32 %27, t27, %33;\n\t"
+      "mul.lo.s32 %28, t28, %33;\n\t"
+      "mul.lo.s32 %29, t29, %33;\n\t"
+      "mul.lo.s32 %30, t30, %33;\n\t"
+      "mul.lo.s32 %31, t31, %33;\n\t"
+      "}"
+      : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]),
+        "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7]),
+        "=r"(w[8]), "=r"(w[9]), "=r"(w[10]), "=r"(w[11]),
+        "=r"(w[12]), "=r"(w[13]), "=r"(w[14]), "=r"(w[15]),
+        "=r"(w[16]), "=r"(w[17]), "=r"(w[18]), "=r"(w[19]),
+        "=r"(w[20]), "=r"(w[21]), "=r"(w[22]), "=r"(w[23]),
+        "=r"(w[24]), "=r"(w[25]), "=r"(w[26]), "=r"(w[27]),
+        "=r"(w[28]), "=r"(w[29]), "=r"(w[30]), "=r"(w[31])
+      : "r"(taddr), "r"(q), "r"(bar)
       : "memory");
 }
 

@@ -11,7 +11,7 @@
 //     out = dtype(float(sum_k a*b) * alpha) with alpha per tensor, or
 //     per-token x per-expert (extension).
 //
-// Structure (one CTA per SM, 20 warps; tiles of 128 rows x 256 columns):
+// Structure (one CTA per SM; tiles of 128 rows x 256 columns):
 //   warp 0      TMA producer: A tile [128 rows x 128 K] and B tile
 //               [BN x 128 K] per K-tile, 128-byte swizzle, into a STAGES-deep
 //               shared-memory ring guarded by full/empty mbarriers.
@@ -22,18 +22,21 @@
 //               the smem stage and, at the end of a quant block, signals the
 //               epilogue.
 //   warps 2, 3  idle (they complete warpgroup 0, which hands its registers
-//               to the epilogue: setmaxnreg 32 there, 112 in the epilogue)
-//   warps 4..19 epilogue: TMEM lane quadrant = warp % 4, column quarter =
-//               (warp - 4) / 4.  Each thread owns one output row and 64
-//               columns: tcgen05.ld the block partial in 16-column chunks
-//               (other warps' accumulation covers each load's latency),
-//               release the TMEM buffer, W += q * P (int32 IMAD); after the
-//               last block convert, scale, round and store the row with 16-B
-//               stores (rows beyond the expert are not stored, so
-//               neighbouring experts are never overwritten).
+//               to the epilogue through setmaxnreg)
+//   warps 4..   epilogue: TMEM lane quadrant = warp % 4, column group =
+//               (warp - 4) / 4.  Each thread owns one output row and 128
+//               columns (8 epilogue warps, 232 registers a thread; CTA pairs:
+//               16 warps of 64 columns at 112): tcgen05.ld the block partial
+//               in 32-column chunks, release the TMEM buffer after the last
+//               load, W += q * P (int32 IMAD); after the last block convert,
+//               scale, round and store the row through shared-memory staging
+//               and TMA tensor stores (rows beyond the expert are not
+//               stored, so neighbouring experts are never overwritten).
 //               The hybrid format costs one integer multiply-add per output
-//               element per quant block, which at 128-deep blocks matches the
-//               tensor-core rate; 16 warps keep that pipe fed.
+//               element per quant block, about the tensor-core rate at
+//               128-deep blocks, so the epilogue's instruction issue, not the
+//               MMA, sets the pace: fewer, wider warps issue fewer
+//               per-block instructions for the same multiply-adds.
 // Tiles: (expert, 128-row m-tile, BN-col n-tile), m-tile major, walked
 // round-robin by the persistent CTAs; the per-expert m-tile prefix is built
 // in shared memory from problem_sizes at kernel start (no host loop, no
@@ -73,17 +76,36 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 128;  // bytes == int8 elements per K-tile
 constexpr int NACC = 2;
-constexpr int kEpiWarps = 16;
-// Warps 0-3 (one warpgroup): TMA producer, MMA issuer, two idle; warps 4-19:
-// epilogue.  Launched at kRegsLaunch registers a thread, the first
-// warpgroup gives registers back (setmaxnreg.dec to kRegsLow) and the four
-// epilogue warpgroups take them (setmaxnreg.inc to kRegsHigh):
+// Warps 0-3 (one warpgroup): TMA producer, MMA issuer, two idle; then the
+// epilogue warps.  Launched at Epi::kRegsLaunch registers a thread, the
+// first warpgroup gives registers back (setmaxnreg.dec to kRegsLow) and the
+// epilogue warpgroups take them (setmaxnreg.inc to kRegsHigh); CTA pairs:
 // 20 warps x 32 x 96 = 128 x 32 + 512 x 112 registers exactly.
 constexpr int kEpiW0 = 4;
-constexpr int kThreads = 32 * kEpiW0 + 32 * kEpiWarps;  // 640
-constexpr int kRegsLaunch = 96, kRegsLow = 32, kRegsHigh = 112;
-static_assert(kThreads * kRegsLaunch == 32 * kEpiW0 * kRegsLow + 32 * kEpiWarps * kRegsHigh,
-              "register split must use exactly the registers the block is launched with");
+constexpr int kEpiWarps = 16;  // epilogue warps of the CTA-pair kernels
+
+// The one-CTA store epilogue runs 8 wide epilogue warps instead: each
+// thread owns one row and 128 accumulator columns (two 64-column
+// weight-scale blocks).  Half as many warps issue half as many per-block
+// instructions (barrier waits, fences, loop control) for the same int32
+// multiply-adds, and at 232 registers a thread the 128 running sums fit
+// beside a 32-column load.  12 warps x 32 x 168 = 128 x 40 + 256 x 232
+// registers.  The fused SiLU epilogue keeps 16 warps of 64 columns: its
+// per-tile SiLU / requant phase is latency-bound and wide warps made it
+// slower (w13 at the default shape 336 against 314 us); so do CTA pairs.
+template <int EPI, int CG>
+struct Epi {
+  static constexpr bool kWide = EPI == 0 && CG == 1;  // EPI 0: kEpiStore
+  static constexpr int kWarps = kWide ? 8 : kEpiWarps;
+  static constexpr int kCols = kWide ? 128 : 64;  // accumulator columns a thread
+  static constexpr int kThreads = 32 * kEpiW0 + 32 * kWarps;
+  static constexpr int kRegsLaunch = kWide ? 168 : 96;
+  static constexpr int kRegsLow = kWide ? 40 : 32;
+  static constexpr int kRegsHigh = kWide ? 232 : 112;
+  static_assert(kThreads * kRegsLaunch == 32 * kEpiW0 * kRegsLow + 32 * kWarps * kRegsHigh,
+                "register split must use exactly the registers the block is launched with");
+  static_assert(kRegsLaunch * kThreads <= 65536, "register file");
+};
 constexpr int kMaxExperts = 1024;
 constexpr int kTileABytes = BM * BK;
 constexpr uint32_t kTmemCols = NACC * BN;
@@ -134,15 +156,18 @@ struct GemmParams {
   int kb_act;
 };
 
-template <int CG>
+template <int CG, int EPI>
 struct SmemLayout {
   static constexpr int kStages = Cfg<CG>::kStages;
+  static constexpr int kWarps = Epi<EPI, CG>::kWarps;
   static constexpr int kA = 0;
   static constexpr int kB = kA + kStages * kTileABytes;
-  // per-epilogue-warp output staging (32 rows x 64 B, 64-byte swizzle)
+  // per-epilogue-warp output staging (32 rows x 64 B, 64-byte swizzle; two
+  // such buffers for the wide warps)
   static constexpr int kStg = kB + kStages * Cfg<CG>::kTileBBytes;  // 1024-B aligned
-  static constexpr int kStgWarpBytes = 32 * 64;
-  static constexpr int kBar = kStg + kEpiWarps * kStgWarpBytes;  // 8-B aligned
+  static constexpr int kStgBufBytes = 32 * 64;
+  static constexpr int kStgWarpBytes = Epi<EPI, CG>::kWide ? 2 * kStgBufBytes : kStgBufBytes;
+  static constexpr int kBar = kStg + kWarps * kStgWarpBytes;  // 8-B aligned
   // full/empty ring, accumulator full/empty, final drain, and the two
   // row-group absmax barriers of the fused SiLU-quant epilogue
   static constexpr int kNumBars = 2 * kStages + 2 * NACC + 1 + 2;
@@ -152,7 +177,7 @@ struct SmemLayout {
   // F_B(up) of the current tile), then the per-expert tables: m-tile prefix,
   // scale-row offset, row count, first row
   static constexpr int kSlots = kRed + 32;
-  static constexpr int kSlotArray = 4 * 32 * kEpiWarps;
+  static constexpr int kSlotArray = 4 * 32 * kWarps;
   static constexpr int kPrefix = kSlots + 9 * kSlotArray;
   static constexpr int bytes(int E) { return kPrefix + 4 * (E + 1) * 4 + 32; }
 };
@@ -245,11 +270,15 @@ __device__ __forceinline__ TileInfo decode_tile_cta(int t, const int* mt_prefix,
 }
 
 template <int MODE, bool HAS_BIAS, typename OutT, int EPI, int CG>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__((Epi<EPI, CG>::kThreads), 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
-  using SmemLayout = i8moe::SmemLayout<CG>;
+  using SmemLayout = i8moe::SmemLayout<CG, EPI>;
+  using EP = Epi<EPI, CG>;
+  constexpr int kThreads = EP::kThreads;
+  constexpr int kEW = EP::kWarps;     // epilogue warps
+  constexpr bool kWide = EP::kWide;   // 128 accumulator columns a thread
   constexpr int STAGES = Cfg<CG>::kStages;
   constexpr int kTileBBytes = Cfg<CG>::kTileBBytes;
   constexpr uint32_t kIdesc = Cfg<CG>::kIdesc;
@@ -304,13 +333,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(bar_accf + 8 * a, 1);
-      mbar_init(bar_acce + 8 * a, CG * kEpiWarps);  // both CTAs' epilogues release
+      // released by every thread of the wide epilogue, else by lane 0 of
+      // every epilogue warp (of both CTAs of a pair)
+      mbar_init(bar_acce + 8 * a, kWide ? 32 * kEW : CG * kEW);
     }
     mbar_init(bar_final, 1);
     // absmax groups: all 16 epilogue warps (tile_m 128) or the 8 warps of
     // each 64-row half (tile_m 64)
-    mbar_init(bar_red, p.tile_m == 64 ? kEpiWarps / 2 : kEpiWarps);
-    mbar_init(bar_red + 8, p.tile_m == 64 ? kEpiWarps / 2 : kEpiWarps);
+    mbar_init(bar_red, p.tile_m == 64 ? kEW / 2 : kEW);
+    mbar_init(bar_red + 8, p.tile_m == 64 ? kEW / 2 : kEW);
     mbar_fence_init();
   }
   // the other CTA of a pair signals this CTA's barriers: they must be
@@ -337,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kEpiW0) {
   // register split, first warpgroup: gives registers back (the host checked
   // the launch count); each role's code sits inside its warpgroup's branch
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(EP::kRegsLow));
   if (warp == 0) {
     // ================= TMA producer =================
     if (lane == 0) {
@@ -498,27 +529,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   } else {
     // register split, epilogue warpgroups: take the registers given back
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
-    // ================= epilogue (16 warps) =================
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(EP::kRegsHigh));
+    // ================= epilogue (16 or 8 warps) =================
     // TMEM lane quadrant = warp % 4 (hardware rule), column group cq =
-    // (warp - kEpiW0) / 4.  Each thread owns one row and 64 accumulator columns:
-    //   kEpiStore:      tile columns [64cq, 64cq+64), one 64-column weight-
-    //                   scale block, so one Q_A * Q_B factor per quant block;
-    //   kEpiSiluQuant:  gate columns [32cq, +32) and the matching up columns
-    //                   [128+32cq, +32): one Q factor for each half.
-    // Four warps share each SM sub-partition, which keeps the integer
+    // (warp - kEpiW0) / 4.  Each thread owns one row and kCols accumulator
+    // columns:
+    //   kEpiStore, 16 warps:   tile columns [64cq, 64cq+64), one 64-column
+    //                          weight-scale block, one Q_A * Q_B factor;
+    //   kEpiStore, 8 wide warps (one CTA per tile): tile columns
+    //                          [128cq, +128), two weight-scale blocks with
+    //                          one factor each (the second in the "up" slot);
+    //   kEpiSiluQuant:         gate columns [32cq, +32) and the matching up
+    //                          columns [128+32cq, +32): one factor for each.
+    // Four (two) warps share each SM sub-partition, which keeps the integer
     // multiply-add pipe busy while the other warps wait for their TMEM loads.
     const int quad = warp & 3;
     const int cq = (warp - kEpiW0) >> 2;
     const uint32_t t_lane = static_cast<uint32_t>(quad * 32) << 16;
     constexpr bool kFused = EPI == kEpiSiluQuant;
+    constexpr bool kTwoQ = kFused || kWide;  // a second weight-scale factor per block
     auto chunk_col = [&](int c) -> uint32_t {  // TMEM column of 16-column chunk c
       if (kFused) return (c < 2) ? 32 * cq + 16 * c : 128 + 32 * cq + 16 * (c - 2);
-      return 64 * cq + 16 * c;
+      return EP::kCols * cq + 16 * c;
     };
     // first output column of this thread in tile t (w13 gate column when fused)
     auto first_col = [&](const TileInfo& u) -> int {
-      return kFused ? u.nt * 128 + 32 * cq : u.nt * BN + 64 * cq;
+      return kFused ? u.nt * 128 + (EP::kCols / 2) * cq : u.nt * BN + EP::kCols * cq;
+    };
+    // the column of the second weight-scale factor's block: the up column
+    // (fused), or the second 64 columns (wide); -1 past the output
+    auto second_col = [&](int col) -> int {
+      if (kFused) return p.n_act + col;
+      return col + 64 < p.N ? col + 64 : -1;
     };
     auto col_valid = [&](int col) -> bool { return col < (kFused ? p.n_act : p.N); };
     int acc = 0;
@@ -548,15 +590,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
     };
     // Q_A * Q_B of quant block (qb0 + lane) of tile t, synchronously (only
-    // for more than 32 quant blocks); `up` selects the up half when fused
-    auto tile_q = [&](int t, int qb0, bool up) -> int {
+    // for more than 32 quant blocks); `second` selects the second factor
+    auto tile_q = [&](int t, int qb0, bool second) -> int {
       const TileInfo u = decode_tile_cta<CG>(t, mt_prefix, p.E, p.n_tiles, rank);
       const int wrow = u.mt * BM + quad * 32;
       const int col = first_col(u);
       const int qb = qb0 + lane;
       if (MODE != kHybrid || wrow >= m_rows[u.e] || !col_valid(col) || qb >= p.nq) return 0;
       const int srow = so_prefix[u.e] + wrow / p.tile_m;
-      const int jb = (up ? p.n_act + col : col) / 64;
+      const int c2 = second ? second_col(col) : col;
+      if (c2 < 0) return 0;
+      const int jb = c2 / 64;
       return __ldg(p.qa + static_cast<int64_t>(srow) * p.q_stride + qb) *
              __ldg(p.qb + (static_cast<int64_t>(u.e) * p.nsb + jb) * p.q_stride + qb);
     };
@@ -575,14 +619,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int32_t* qb_e = p.qb + static_cast<int64_t>(u.e) * p.nsb * p.q_stride + qb;
           cp_async4(s_qa, p.qa + static_cast<int64_t>(srow) * p.q_stride + qb);
           cp_async4(s_qb, qb_e + static_cast<int64_t>(col / 64) * p.q_stride);
-          if (kFused) cp_async4(s_qbu, qb_e + static_cast<int64_t>((p.n_act + col) / 64) * p.q_stride);
+          if (kTwoQ) {
+            const int c2 = second_col(col);
+            if (c2 >= 0)
+              cp_async4(s_qbu, qb_e + static_cast<int64_t>(c2 / 64) * p.q_stride);
+            else
+              st_s32(s_qbu, 0);
+          }
           any = true;
         }
       }
       if (!any) {
         st_s32(s_qa, 0);
         st_s32(s_qb, 0);
-        if (kFused) st_s32(s_qbu, 0);
+        if (kTwoQ) st_s32(s_qbu, 0);
       }
     };
     fetch_q(tile0, 0);
@@ -595,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t s_qa = s_slot + (3 * par) * kSA;
         const int qa = ld_s32(s_qa);
         qv = qa * ld_s32(s_qa + kSA);
-        if (kFused) qvu = qa * ld_s32(s_qa + 2 * kSA);
+        if (kTwoQ) qvu = qa * ld_s32(s_qa + 2 * kSA);
       }
       fetch_q(t + tstride, par ^ 1);
       // CG == 2: this CTA's half of the pair tile may lie past the expert's
@@ -612,18 +662,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float* fb_e = p.fb + static_cast<int64_t>(ti.e) * p.nsb * p.f_stride;
           cp_async4(s_fa, p.fa + static_cast<int64_t>(srow) * p.f_stride);
           cp_async4(s_fb, fb_e + static_cast<int64_t>(col0 / 64) * p.f_stride);
-          if (kFused) cp_async4(s_fbu, fb_e + static_cast<int64_t>((p.n_act + col0) / 64) * p.f_stride);
+          if (kTwoQ) {
+            const int c2 = second_col(col0);
+            if (c2 >= 0) cp_async4(s_fbu, fb_e + static_cast<int64_t>(c2 / 64) * p.f_stride);
+          }
         }
       }
-      int32_t W[64];
+      int32_t W[EP::kCols];
       // The store epilogue writes its sums with the first quant block
-      // (W = q * P) and takes chunks 0-2 through tmem_mad16 / tmem_mul16,
-      // whose loaded values never become C variables: that keeps its 64 sums
-      // in registers without spills (w2 at the default shape: 211 -> 200 us).
-      // The fused SiLU epilogue keeps the plain form, which spills less there.
+      // (W = q * P) and takes its chunks through asm blocks (tmem_mad16 /
+      // tmem_mul16, or the 32-column forms for the wide warps) whose loaded
+      // values never become C variables: that keeps the sums in registers
+      // without spills.  The fused SiLU epilogue keeps the plain form, which
+      // spills less there.
       if (kFused || p.nq == 0) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) W[i] = 0;
+        for (int i = 0; i < EP::kCols; ++i) W[i] = 0;
       }
       // One 16-column chunk in flight per warp: with four epilogue warps on
       // each SM sub-partition the other warps' multiply-adds cover the TMEM
@@ -633,10 +687,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t P[16];
       for (int qb = 0; qb < p.nq && ok; ++qb) {
         const int q = __shfl_sync(0xffffffffu, qv, qb & 31);
-        const int qu = kFused ? __shfl_sync(0xffffffffu, qvu, qb & 31) : 0;
+        const int qu = kTwoQ ? __shfl_sync(0xffffffffu, qvu, qb & 31) : 0;
         if ((qb & 31) == 31 && qb + 1 < p.nq) {  // K > 4096: the next 32 factors
           qv = tile_q(t, qb + 1, false);
-          if (kFused) qvu = tile_q(t, qb + 1, true);
+          if (kTwoQ) qvu = tile_q(t, qb + 1, true);
         }
         if (!mbar_wait(bar_accf + 8 * acc, aphase, s_abort, &g_err_gemm, kErrEpilogueTimeout)) {
           ok = false;
@@ -650,6 +704,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++acc == NACC) acc = 0, aphase ^= 1;
           continue;
         }
+        if constexpr (kWide) {
+          // four 32-column chunks of tile columns [128cq, +128), q for the
+          // first 64 columns, qu for the other 64.  Each chunk is one asm
+          // block (load, wait, 32 multiply-adds) whose
+          // loaded values never become C variables; the last one hands the
+          // accumulator back as soon as its load has landed (every thread
+          // arrives).  Double-buffering the loads through C arrays measured
+          // slower (w2 206 against 190 us).
+          const uint32_t tb0 = tmem_base + t_lane + acc * BN + 128 * cq;
+          const uint32_t tb1 = tb0 + 64;
+          const uint32_t rb = bar_acce + 8 * acc;
+          const int q0 = MODE == kHybrid ? q : 1;
+          const int q1 = MODE == kHybrid ? qu : 1;
+          if (qb == 0) {
+            tmem_mul32(tb0, q0, 0u, W);
+            tmem_mul32(tb0 + 32, q0, 0u, W + 32);
+            tmem_mul32(tb1, q1, 0u, W + 64);
+            tmem_mul32_release(tb1 + 32, q1, rb, W + 96);
+          } else {
+            tmem_mad32(tb0, q0, 0u, W);
+            tmem_mad32(tb0 + 32, q0, 0u, W + 32);
+            tmem_mad32(tb1, q1, 0u, W + 64);
+            tmem_mad32_release(tb1 + 32, q1, rb, W + 96);
+          }
+          if (++acc == NACC) acc = 0, aphase ^= 1;
+        } else {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           if constexpr (!kFused) {
@@ -692,6 +772,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 16; ++i) W[16 * c + i] += static_cast<int32_t>(P[i]);
           }
         }
+        }  // narrow epilogue
       }
       if (!ok) break;
       if (!own_ok) continue;
@@ -713,10 +794,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool row_ok = lrow < m_e;
         const float* bg = HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0
                                    : nullptr;
-        uint4 act[4];
+        // kAC chunks of 8 activations: the thread's gate columns are W[0, kU)
+        // and the matching up columns W[kU, 2 kU)
+        constexpr int kU = EP::kCols / 2;
+        constexpr int kAC = kU / 8;
+        uint4 act[kAC];
         float m = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kAC; ++j) {
           uint32_t g4[4], u4[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -724,13 +809,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (HAS_BIAS) {
               g4[i] = pack2<OutT>(bias_epi(W[c], fg, __ldg(bg + c)),
                                   bias_epi(W[c + 1], fg, __ldg(bg + c + 1)));
-              u4[i] = pack2<OutT>(bias_epi(W[32 + c], fu, __ldg(bg + p.n_act + c)),
-                                  bias_epi(W[32 + c + 1], fu, __ldg(bg + p.n_act + c + 1)));
+              u4[i] = pack2<OutT>(bias_epi(W[kU + c], fu, __ldg(bg + p.n_act + c)),
+                                  bias_epi(W[kU + c + 1], fu, __ldg(bg + p.n_act + c + 1)));
             } else {
               g4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[c]), fg),
                                   __fmul_rn(static_cast<float>(W[c + 1]), fg));
-              u4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[32 + c]), fu),
-                                  __fmul_rn(static_cast<float>(W[32 + c + 1]), fu));
+              u4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[kU + c]), fu),
+                                  __fmul_rn(static_cast<float>(W[kU + c + 1]), fu));
             }
           }
           uint4 a = silu_mul_chunk<OutT>(make_uint4(g4[0], g4[1], g4[2], g4[3]),
@@ -769,128 +854,156 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int srow = so_prefix[ti.e] + grow0 / p.tile_m;
           p.act_scale[static_cast<int64_t>(srow) * p.kb_act + ti.nt] = scale;
         }
-        uint32_t qw[8];
+        uint32_t qw[2 * kAC];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kAC; ++j) {
           uint2 q2;
           if (!quant_chunk_bracket<OutT>(act[j], qi, q2)) q2 = quant_chunk_exact16<OutT>(act[j], scale);
           qw[2 * j] = q2.x;
           qw[2 * j + 1] = q2.y;
         }
-        if (wrow0 + 32 <= m_e && col0 + 32 <= p.n_act) {
-          // whole warp inside the expert: 32 rows x 32 bytes staged with the
-          // 32-byte swizzle, one TMA tensor store
+        if (wrow0 + 32 <= m_e && col0 + kU <= p.n_act) {
+          // whole warp inside the expert: 32 rows x 32 bytes per TMA tensor
+          // store (kU / 32 of them), staged with the 32-byte swizzle
           const uint32_t stg = sbase + SmemLayout::kStg + (warp - kEpiW0) * SmemLayout::kStgWarpBytes;
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t a = stg + 32 * lane + 16 * (h ^ ((lane >> 2) & 1));
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(qw[4 * h]),
-                         "r"(qw[4 * h + 1]), "r"(qw[4 * h + 2]), "r"(qw[4 * h + 3])
-                         : "memory");
+          for (int s32 = 0; s32 < kU / 32; ++s32) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t a = stg + 1024 * s32 + 32 * lane + 16 * (h ^ ((lane >> 2) & 1));
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                           "r"(qw[8 * s32 + 4 * h]), "r"(qw[8 * s32 + 4 * h + 1]),
+                           "r"(qw[8 * s32 + 4 * h + 2]), "r"(qw[8 * s32 + 4 * h + 3])
+                           : "memory");
+            }
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmO, stg, col0, e_row0[ti.e] + wrow0);
+#pragma unroll
+            for (int s32 = 0; s32 < kU / 32; ++s32)
+              tma_store_2d(&tmO, stg + 1024 * s32, col0 + 32 * s32, e_row0[ti.e] + wrow0);
             bulk_commit();
           }
         } else if (row_ok) {
           int8_t* dst = p.act_q + static_cast<int64_t>(e_row0[ti.e] + lrow) * p.n_act + col0;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
+          for (int j = 0; j < kAC; ++j)
             if (col0 + 8 * j < p.n_act)
               *reinterpret_cast<uint2*>(dst + 8 * j) = make_uint2(qw[2 * j], qw[2 * j + 1]);
         }
         ++lt;
         continue;
       }
-      // ---- convert, scale, round, store ----
-      float f;
+      // ---- convert, scale, round, store (per 64-column half) ----
+      constexpr int kHalves = EP::kCols / 64;
+      float fh[kHalves];
       if (MODE == kHybrid) {
         cp_async_wait_all();
-        f = __int_as_float(ld_s32(s_fa)) * __int_as_float(ld_s32(s_fb));
-      } else if (p.a_row_scale != nullptr) {
-        f = lrow < m_e ? __ldg(p.a_row_scale + e_row0[ti.e] + lrow) * __ldg(p.b_expert_scale + ti.e)
-                       : 0.f;
+        const float fa = __int_as_float(ld_s32(s_fa));
+        fh[0] = fa * __int_as_float(ld_s32(s_fb));
+        if constexpr (kHalves == 2) fh[1] = fa * __int_as_float(ld_s32(s_fbu));
       } else {
-        f = p.alpha;
+        const float f = p.a_row_scale == nullptr
+                            ? p.alpha
+                            : (lrow < m_e ? __ldg(p.a_row_scale + e_row0[ti.e] + lrow) *
+                                                __ldg(p.b_expert_scale + ti.e)
+                                          : 0.f);
+#pragma unroll
+        for (int hh = 0; hh < kHalves; ++hh) fh[hh] = f;
       }
-      if constexpr (!std::is_same<OutT, int32_t>::value) {
-        if (wrow0 + 32 <= m_e && col0 + 64 <= p.N) {
-          // All 32 rows belong to this expert: stage the warp's 32 x 64 block
-          // in shared memory (64-byte swizzle, conflict-free) and write it
-          // with two TMA tensor stores of 32 x 32, so the stores leave as
-          // whole lines instead of 32 row fragments per instruction.
-          const uint32_t stg = sbase + SmemLayout::kStg + (warp - kEpiW0) * SmemLayout::kStgWarpBytes;
-          const float* bp =
-              HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0 : nullptr;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (lane == 0) bulk_wait_read0();  // the previous store has read the buffer
-            __syncwarp();
+      for (int hh = 0; hh < kHalves; ++hh) {
+        const float f = fh[hh];
+        const int colh = col0 + 64 * hh;
+        const int32_t* Wh = W + 64 * hh;
+        if constexpr (!std::is_same<OutT, int32_t>::value) {
+          if (wrow0 + 32 <= m_e && colh + 64 <= p.N) {
+            // All 32 rows belong to this expert: stage the warp's 32 x 64
+            // block in shared memory (64-byte swizzle, conflict-free) and
+            // write it with two TMA tensor stores of 32 x 32, so the stores
+            // leave as whole lines instead of 32 row fragments per
+            // instruction.  Wide warps alternate two staging buffers.
+            const uint32_t stg = sbase + SmemLayout::kStg +
+                                 (warp - kEpiW0) * SmemLayout::kStgWarpBytes +
+                                 hh * SmemLayout::kStgBufBytes;
+            const float* bp =
+                HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + colh : nullptr;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint32_t w4[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int c = 32 * h + 8 * j + 2 * i;
-                if (HAS_BIAS) {
-                  w4[i] = pack2<OutT>(bias_epi(W[c], f, __ldg(bp + c)),
-                                      bias_epi(W[c + 1], f, __ldg(bp + c + 1)));
-                } else {
-                  w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[c]), f),
-                                      __fmul_rn(static_cast<float>(W[c + 1]), f));
-                }
+            for (int h = 0; h < 2; ++h) {
+              // the previous store from this buffer has read it (wide: the
+              // other buffer's latest store may still be reading)
+              if (lane == 0) {
+                if (kWide && h == 0)
+                  bulk_wait_read1();
+                else
+                  bulk_wait_read0();
               }
-              const uint32_t a = stg + 64 * lane + 16 * (j ^ ((lane >> 1) & 3));
-              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w4[0]),
-                           "r"(w4[1]), "r"(w4[2]), "r"(w4[3])
-                           : "memory");
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int c = 32 * h + 8 * j + 2 * i;
+                  if (HAS_BIAS) {
+                    w4[i] = pack2<OutT>(bias_epi(Wh[c], f, __ldg(bp + c)),
+                                        bias_epi(Wh[c + 1], f, __ldg(bp + c + 1)));
+                  } else {
+                    w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(Wh[c]), f),
+                                        __fmul_rn(static_cast<float>(Wh[c + 1]), f));
+                  }
+                }
+                const uint32_t a = stg + 64 * lane + 16 * (j ^ ((lane >> 1) & 3));
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w4[0]),
+                             "r"(w4[1]), "r"(w4[2]), "r"(w4[3])
+                             : "memory");
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmO, stg, colh + 32 * h, e_row0[ti.e] + wrow0);
+                bulk_commit();
+              }
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmO, stg, col0 + 32 * h, e_row0[ti.e] + wrow0);
-              bulk_commit();
-            }
+            continue;
           }
-          continue;
         }
-      }
-      if (!(lrow < m_e && col0 < p.N)) continue;
-      const int64_t row_off = static_cast<int64_t>(e_row0[ti.e] + lrow) * p.N + col0;
-      const int ncols = min(64, p.N - col0);
-      if constexpr (std::is_same<OutT, int32_t>::value) {
-        // raw accumulator output (verification mode)
-        int32_t* dst = static_cast<int32_t*>(p.out) + row_off;
-        (void)f;
+        if (!(lrow < m_e && colh < p.N)) continue;
+        const int64_t row_off = static_cast<int64_t>(e_row0[ti.e] + lrow) * p.N + colh;
+        const int ncols = min(64, p.N - colh);
+        if constexpr (std::is_same<OutT, int32_t>::value) {
+          // raw accumulator output (verification mode)
+          int32_t* dst = static_cast<int32_t*>(p.out) + row_off;
+          (void)f;
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-          if (4 * c < ncols)
-            *reinterpret_cast<int4*>(dst + 4 * c) =
-                make_int4(W[4 * c], W[4 * c + 1], W[4 * c + 2], W[4 * c + 3]);
-      } else {
-        OutT* dst = static_cast<OutT*>(p.out) + row_off;
-        const float* bp = HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + col0
-                                   : nullptr;
+          for (int c = 0; c < 16; ++c)
+            if (4 * c < ncols)
+              *reinterpret_cast<int4*>(dst + 4 * c) =
+                  make_int4(Wh[4 * c], Wh[4 * c + 1], Wh[4 * c + 2], Wh[4 * c + 3]);
+        } else {
+          OutT* dst = static_cast<OutT*>(p.out) + row_off;
+          const float* bp =
+              HAS_BIAS ? p.bias + static_cast<int64_t>(ti.e) * p.bias_stride + colh : nullptr;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (8 * c >= ncols) continue;
-          uint32_t w4[4];
+          for (int c = 0; c < 8; ++c) {
+            if (8 * c >= ncols) continue;
+            uint32_t w4[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int j = 8 * c + 2 * i;
-            if (HAS_BIAS) {
-              w4[i] = pack2<OutT>(bias_epi(W[j], f, __ldg(bp + j)),
-                                  bias_epi(W[j + 1], f, __ldg(bp + j + 1)));
-            } else {
-              w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(W[j]), f),
-                                  __fmul_rn(static_cast<float>(W[j + 1]), f));
+            for (int i = 0; i < 4; ++i) {
+              const int j = 8 * c + 2 * i;
+              if (HAS_BIAS) {
+                w4[i] = pack2<OutT>(bias_epi(Wh[j], f, __ldg(bp + j)),
+                                    bias_epi(Wh[j + 1], f, __ldg(bp + j + 1)));
+              } else {
+                w4[i] = pack2<OutT>(__fmul_rn(static_cast<float>(Wh[j]), f),
+                                    __fmul_rn(static_cast<float>(Wh[j + 1]), f));
+              }
             }
+            *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
-          *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
     }
@@ -998,8 +1111,9 @@ template <int MODE, bool HAS_BIAS, typename OutT, int EPI, int CG>
 int launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
               const GemmParams& p, int64_t upper_tiles, cudaStream_t st) {
   auto kern = grouped_gemm_kernel<MODE, HAS_BIAS, OutT, EPI, CG>;
-  const int smem = SmemLayout<CG>::bytes(p.E) + 1024;
-  const int smem_max = std::min(SmemLayout<CG>::bytes(kMaxExperts) + 1024, kSmemLimit);
+  using EP = Epi<EPI, CG>;
+  const int smem = SmemLayout<CG, EPI>::bytes(p.E) + 1024;
+  const int smem_max = std::min(SmemLayout<CG, EPI>::bytes(kMaxExperts) + 1024, kSmemLimit);
   if (smem > smem_max) return set_error(I8MOE_ERR_UNSUPPORTED, "grouped GEMM: too many experts");
   static int attr_done[64] = {0};
   static int max_clusters[64] = {0};
@@ -1011,9 +1125,9 @@ int launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
     // epilogue's setmaxnreg.inc waiting (fewer) or fail to launch (more)
     cudaFuncAttributes fa;
     I8_CUDA(cudaFuncGetAttributes(&fa, kern));
-    I8_REQUIRE(fa.numRegs == kRegsLaunch,
+    I8_REQUIRE(fa.numRegs == EP::kRegsLaunch,
                "grouped GEMM: compiled with %d registers a thread; its register split needs %d",
-               fa.numRegs, kRegsLaunch);
+               fa.numRegs, EP::kRegsLaunch);
     I8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
     if (CG == 2) {
       cudaLaunchConfig_t q = {};
@@ -1023,7 +1137,7 @@ int launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
       qa[0].val.clusterDim.y = 1;
       qa[0].val.clusterDim.z = 1;
       q.gridDim = dim3(2 * static_cast<unsigned>(num_sms(dev) / 2));
-      q.blockDim = dim3(kThreads);
+      q.blockDim = dim3(EP::kThreads);
       q.dynamicSmemBytes = smem_max;
       q.attrs = qa;
       q.numAttrs = 1;
@@ -1046,7 +1160,7 @@ int launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * static_cast<unsigned>(pairs));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(EP::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
@@ -1054,7 +1168,7 @@ int launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
     I8_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, p));
   } else {
     const int grid = static_cast<int>(std::min<int64_t>(num_sms(dev), std::max<int64_t>(upper_tiles, 1)));
-    kern<<<grid, kThreads, smem, st>>>(ta, tb, to, p);
+    kern<<<grid, EP::kThreads, smem, st>>>(ta, tb, to, p);
   }
   return check_launch("grouped_gemm_kernel");
 }
@@ -1064,7 +1178,10 @@ int g_cta_pairs = -1;
 
 // the pair layout's five-stage ring leaves room for the per-expert tables
 // of up to ~700 experts within the 227 KB a CTA may use
-bool pairs_fit(int64_t E) { return SmemLayout<2>::bytes(static_cast<int>(E)) + 1024 <= kSmemLimit; }
+bool pairs_fit(int64_t E) {
+  return SmemLayout<2, kEpiStore>::bytes(static_cast<int>(E)) + 1024 <= kSmemLimit &&
+         SmemLayout<2, kEpiSiluQuant>::bytes(static_cast<int>(E)) + 1024 <= kSmemLimit;
+}
 
 // Pair tiles cover 256 rows of one expert, so an expert with an odd number
 // of 128-row m-tiles leaves half of its last pair tile idle.  Measured on
